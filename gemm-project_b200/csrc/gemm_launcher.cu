@@ -1,0 +1,445 @@
+// C-ABI entry points and shape/alignment dispatch for the B200 FP16 GEMM.
+//
+// Drop-in for the reference launcher src/gemm.cu:18-134: same exported symbol
+// and semantics (row-major FP16, FP32 accumulation, alpha/beta epilogue, C not
+// read when beta == 0, M<=0 or N<=0 is a no-op, asynchronous on the default
+// stream). The dispatch keeps the reference's principle (choose by dimensions
+// and pointer alignment, src/gemm.cu:20-24 and :112-133) but routes to sm_100a
+// kernels:
+//   K <= 0                      -> scale_c_kernel (C = beta*C)
+//   M <= 8                      -> rows_gemv_kernel<MR>  (HBM streaming, cluster split-K)
+//   N == 1                      -> col_gemv_kernel       (HBM streaming)
+//   otherwise                   -> tc_gemm_kernel<BN>    (tcgen05 + TMA + TMEM)
+// The tcgen05 path needs TMA-addressable operands (16-byte aligned base, row
+// pitch a multiple of 16 bytes). An operand that is not (K % 8 != 0, N % 8 != 0
+// or a base offset by one half, the reference's misaligned cases) is first
+// repacked into a stream-ordered scratch buffer with an aligned pitch; C is
+// written in place with per-element predication, so it may be misaligned.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/gemm_b200.h"
+#include "ptx.cuh"
+#include "skinny.cuh"
+#include "tc_gemm.cuh"
+
+namespace gemm_b200 {
+
+__device__ int g_device_error;
+
+// Test-only kernel: waits on an mbarrier that nothing completes, bounded.
+__global__ void wait_probe_kernel(unsigned long long timeout_ns, int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_wait(smem_u32(&bar), 0, timeout_ns, &abort_flag, err, kErrTimeoutProbe);
+  }
+  __syncthreads();
+}
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+thread_local int tl_status = 0;
+thread_local const char* tl_last_kernel = "";
+
+struct DeviceInfo {
+  int sms = 0;
+  int* err = nullptr;
+  bool configured = false;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mutex;
+
+void record_error(cudaError_t e) {
+  if (e != cudaSuccess && tl_status == 0) tl_status = static_cast<int>(e);
+}
+
+bool launch_log_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("GEMM_LAUNCH_LOG");
+    return !(v && (std::strcmp(v, "0") == 0 || std::strcmp(v, "off") == 0));
+  }();
+  return on;
+}
+
+unsigned long long wait_timeout_ns() {
+  static const unsigned long long ns = [] {
+    const char* v = std::getenv("GEMM_WAIT_TIMEOUT_MS");
+    long long ms = v ? std::atoll(v) : 2000;
+    if (ms <= 0) ms = 2000;
+    return static_cast<unsigned long long>(ms) * 1000000ull;
+  }();
+  return ns;
+}
+
+void log_launch(const char* kernel, int M, int N, int K, dim3 grid, dim3 block) {
+  tl_last_kernel = kernel;
+  if (!launch_log_enabled()) return;
+  std::printf("Launching %s: M=%d N=%d K=%d, grid=(%u,%u,%u), block=(%u,%u,%u)\n", kernel, M, N, K,
+              grid.x, grid.y, grid.z, block.x, block.y, block.z);
+  std::fflush(stdout);
+}
+
+template <int BN>
+void configure_tc() {
+  cudaFuncSetAttribute(tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       TcCfg<BN>::kSmemBytes);
+}
+
+// Per-device one-time set-up: SM count, device error word, kernel attributes.
+DeviceInfo& device_info() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  DeviceInfo& d = g_dev[dev % kMaxDevices];
+  if (d.configured) return d;
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  if (!d.configured) {
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    void* p = nullptr;
+    record_error(cudaGetSymbolAddress(&p, g_device_error));
+    d.err = static_cast<int*>(p);
+    configure_tc<64>();
+    configure_tc<128>();
+    configure_tc<256>();
+    std::atomic_thread_fence(std::memory_order_release);
+    d.configured = true;
+  }
+  return d;
+}
+
+// ---------------------------------------------------------------------------
+// TMA descriptors through the driver entry point (no link-time libcuda).
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// 2-D FP16 tensor map, 128B swizzle, zero fill out of bounds.
+bool make_tmap(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+               uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {pitch_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+inline int round_up8(int v) { return (v + 7) / 8 * 8; }
+
+// ---------------------------------------------------------------------------
+// Paths
+// ---------------------------------------------------------------------------
+void launch_scale(half* C, int M, int N, float beta, cudaStream_t s, const DeviceInfo& d) {
+  const size_t count = static_cast<size_t>(M) * N;
+  const int blocks = static_cast<int>(std::min<size_t>((count + 255) / 256, size_t(d.sms) * 8));
+  log_launch("scale_c_kernel", M, N, 0, dim3(blocks), dim3(256));
+  scale_c_kernel<<<blocks, 256, 0, s>>>(C, count, beta);
+  record_error(cudaGetLastError());
+}
+
+int choose_tile_n(int M, int N, int sms) {
+  const int tiles_m = ceil_div(M, 128);
+  const int cand[3] = {256, 128, 64};
+  const float eff[3] = {1.0f, 0.9f, 0.65f};
+  int best = 256;
+  float best_cost = 1e30f;
+  for (int i = 0; i < 3; ++i) {
+    const int tiles = tiles_m * ceil_div(N, cand[i]);
+    const int waves = ceil_div(tiles, sms);
+    const float cost = waves * cand[i] / eff[i];
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = cand[i];
+    }
+  }
+  return best;
+}
+
+template <int BN>
+void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, int sms,
+                  cudaStream_t s, int M, int N, int K) {
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = std::min(tiles, sms);
+  static const char* names[3] = {"tc_gemm_kernel<128x64>", "tc_gemm_kernel<128x128>",
+                                 "tc_gemm_kernel<128x256>"};
+  log_launch(names[BN == 64 ? 0 : (BN == 128 ? 1 : 2)], M, N, K, dim3(grid),
+             dim3(TcCfg<BN>::kThreads));
+  tc_gemm_kernel<BN><<<grid, TcCfg<BN>::kThreads, TcCfg<BN>::kSmemBytes, s>>>(ta, tb, p);
+  record_error(cudaGetLastError());
+}
+
+int launch_tc(const half* A, const half* B, half* C, int M, int N, int K, float alpha, float beta,
+              cudaStream_t s, int tile_n, const DeviceInfo& d) {
+  const bool a_ok = aligned16(A) && K % 8 == 0;
+  const bool b_ok = aligned16(B) && N % 8 == 0;
+  const half* a_src = A;
+  const half* b_src = B;
+  int lda = K, ldb = N;
+  void* scratch = nullptr;
+  size_t a_bytes = 0, b_bytes = 0;
+  if (!a_ok) a_bytes = static_cast<size_t>(M) * round_up8(K) * sizeof(half);
+  if (!b_ok) b_bytes = static_cast<size_t>(K) * round_up8(N) * sizeof(half);
+  a_bytes = (a_bytes + 255) / 256 * 256;
+  if (a_bytes + b_bytes) {
+    cudaError_t e = cudaMallocAsync(&scratch, a_bytes + b_bytes, s);
+    if (e != cudaSuccess) {
+      record_error(e);
+      return -1;
+    }
+    const int threads = 256;
+    if (!a_ok) {
+      lda = round_up8(K);
+      half* dst = static_cast<half*>(scratch);
+      const size_t work = static_cast<size_t>(M) * ceil_div(K, 8);
+      const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
+      log_launch("pack_rows_kernel<A>", M, N, K, dim3(blocks), dim3(threads));
+      pack_rows_kernel<<<blocks, threads, 0, s>>>(A, K, dst, lda, M, K);
+      record_error(cudaGetLastError());
+      a_src = dst;
+    }
+    if (!b_ok) {
+      ldb = round_up8(N);
+      half* dst = reinterpret_cast<half*>(static_cast<char*>(scratch) + a_bytes);
+      const size_t work = static_cast<size_t>(K) * ceil_div(N, 8);
+      const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
+      log_launch("pack_rows_kernel<B>", M, N, K, dim3(blocks), dim3(threads));
+      pack_rows_kernel<<<blocks, threads, 0, s>>>(B, N, dst, ldb, K, N);
+      record_error(cudaGetLastError());
+      b_src = dst;
+    }
+  }
+
+  int bn = tile_n ? tile_n : choose_tile_n(M, N, d.sms);
+  CUtensorMap ta, tb;
+  bool ok = make_tmap(&ta, a_src, K, M, static_cast<uint64_t>(lda) * 2, 64, 128) &&
+            make_tmap(&tb, b_src, N, K, static_cast<uint64_t>(ldb) * 2, 64, 64);
+  if (!ok) {
+    record_error(cudaErrorInvalidValue);
+    if (scratch) cudaFreeAsync(scratch, s);
+    return -1;
+  }
+  TcParams p{};
+  p.C = C;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = N;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.tiles_m = ceil_div(M, 128);
+  p.tiles_n = ceil_div(N, bn);
+  p.num_kb = ceil_div(K, 64);
+  p.group = std::min(p.tiles_m, 8);
+  p.c_vec_ok = aligned16(C) && N % 8 == 0;
+  p.timeout_ns = wait_timeout_ns();
+  p.err = d.err;
+  switch (bn) {
+    case 64: launch_tc_bn<64>(ta, tb, p, d.sms, s, M, N, K); break;
+    case 128: launch_tc_bn<128>(ta, tb, p, d.sms, s, M, N, K); break;
+    default: launch_tc_bn<256>(ta, tb, p, d.sms, s, M, N, K); break;
+  }
+  if (scratch) cudaFreeAsync(scratch, s);
+  return 0;
+}
+
+template <int MR, bool VEC>
+void launch_rows_mr(const SkinnyParams& p, int strips, cudaStream_t s, int M, int N, int K) {
+  static const char* names_vec[4] = {"rows_gemv_kernel<1>", "rows_gemv_kernel<2>",
+                                     "rows_gemv_kernel<4>", "rows_gemv_kernel<8>"};
+  static const char* names_sca[4] = {"rows_gemv_kernel<1,scalar>", "rows_gemv_kernel<2,scalar>",
+                                     "rows_gemv_kernel<4,scalar>", "rows_gemv_kernel<8,scalar>"};
+  const int idx = MR == 1 ? 0 : (MR == 2 ? 1 : (MR == 4 ? 2 : 3));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(strips, p.ksplit, 1);
+  cfg.blockDim = dim3(kSkinnyThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = p.ksplit;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  log_launch(VEC ? names_vec[idx] : names_sca[idx], M, N, K, cfg.gridDim, cfg.blockDim);
+  record_error(cudaLaunchKernelEx(&cfg, rows_gemv_kernel<MR, VEC>, p));
+}
+
+int launch_rows(const half* A, const half* B, half* C, int M, int N, int K, float alpha,
+                float beta, cudaStream_t s, const DeviceInfo& d) {
+  if (M > 8) return -1;
+  SkinnyParams p{};
+  p.A = A;
+  p.B = B;
+  p.C = C;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.alpha = alpha;
+  p.beta = beta;
+  const bool vec = (N % 8 == 0);
+  // Element phase of B inside its 16-byte line; identical for every row when N % 8 == 0.
+  p.phase = vec ? static_cast<int>((reinterpret_cast<uintptr_t>(B) / 2) % 8) : 0;
+  p.groups = ceil_div(N + p.phase, 8);
+  const int strips = ceil_div(p.groups, 32);
+  const int target = d.sms * 8;
+  int ksplit = 1;
+  while (ksplit < 8 && strips * ksplit * 2 <= target && K / (ksplit * 2) >= 256) ksplit *= 2;
+  p.ksplit = ksplit;
+  p.kchunk = ceil_div(K, ksplit);
+  p.timeout_ns = wait_timeout_ns();
+  p.err = d.err;
+  const int mr = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
+  if (vec) {
+    switch (mr) {
+      case 1: launch_rows_mr<1, true>(p, strips, s, M, N, K); break;
+      case 2: launch_rows_mr<2, true>(p, strips, s, M, N, K); break;
+      case 4: launch_rows_mr<4, true>(p, strips, s, M, N, K); break;
+      default: launch_rows_mr<8, true>(p, strips, s, M, N, K); break;
+    }
+  } else {
+    switch (mr) {
+      case 1: launch_rows_mr<1, false>(p, strips, s, M, N, K); break;
+      case 2: launch_rows_mr<2, false>(p, strips, s, M, N, K); break;
+      case 4: launch_rows_mr<4, false>(p, strips, s, M, N, K); break;
+      default: launch_rows_mr<8, false>(p, strips, s, M, N, K); break;
+    }
+  }
+  return 0;
+}
+
+int launch_col(const half* A, const half* B, half* C, int M, int N, int K, float alpha, float beta,
+               cudaStream_t s, const DeviceInfo& d) {
+  if (N != 1) return -1;
+  ColParams p{};
+  p.A = A;
+  p.B = B;
+  p.C = C;
+  p.M = M;
+  p.K = K;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.vec = aligned16(A) && aligned16(B) && K % 8 == 0;
+  const int warps_target = d.sms * 64;
+  p.rows_per_warp = std::max(1, ceil_div(M, warps_target));
+  const int warps = ceil_div(M, p.rows_per_warp);
+  const int blocks = ceil_div(warps, 8);
+  log_launch(p.vec ? "col_gemv_kernel" : "col_gemv_kernel<scalar>", M, N, K, dim3(blocks), dim3(256));
+  col_gemv_kernel<<<blocks, 256, 0, s>>>(p);
+  record_error(cudaGetLastError());
+  return 0;
+}
+
+int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float alpha, float beta,
+             cudaStream_t s, int path, int tile_n) {
+  if (M <= 0 || N <= 0) return 0;
+  DeviceInfo& d = device_info();
+  if (K <= 0) {
+    launch_scale(C, M, N, beta, s, d);
+    return 0;
+  }
+  if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256) return -1;
+  if (path == 0) {
+    if (M <= 8)
+      path = 2;
+    else if (N == 1)
+      path = 3;
+    else
+      path = 1;
+  }
+  switch (path) {
+    case 1: return launch_tc(A, B, C, M, N, K, alpha, beta, s, tile_n, d);
+    case 2: return launch_rows(A, B, C, M, N, K, alpha, beta, s, d);
+    case 3: return launch_col(A, B, C, M, N, K, alpha, beta, s, d);
+    default: return -1;
+  }
+}
+
+}  // namespace
+}  // namespace gemm_b200
+
+using namespace gemm_b200;
+
+extern "C" GEMM_API void gemm_launcher(const half* A, const half* B, half* C, int M, int N, int K,
+                              float alpha, float beta) {
+  dispatch(A, B, C, M, N, K, alpha, beta, /*stream=*/0, 0, 0);
+}
+
+extern "C" GEMM_API void gemm_launcher_stream(const half* A, const half* B, half* C, int M, int N, int K,
+                                     float alpha, float beta, cudaStream_t stream) {
+  dispatch(A, B, C, M, N, K, alpha, beta, stream, 0, 0);
+}
+
+extern "C" GEMM_API int gemm_launcher_ex(const half* A, const half* B, half* C, int M, int N, int K,
+                                float alpha, float beta, cudaStream_t stream, int path,
+                                int tile_n) {
+  return dispatch(A, B, C, M, N, K, alpha, beta, stream, path, tile_n);
+}
+
+extern "C" GEMM_API int gemm_launcher_status(void) {
+  int status = tl_status;
+  tl_status = 0;
+  int dev_err = 0;
+  if (cudaMemcpyFromSymbol(&dev_err, g_device_error, sizeof(int)) == cudaSuccess && dev_err) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    if (status == 0) status = 1000 + dev_err;
+  }
+  return status;
+}
+
+extern "C" GEMM_API const char* gemm_last_kernel(void) { return tl_last_kernel; }
+
+extern "C" GEMM_API int gemm_slab_rows(int M, int world, int rank, int* row0) {
+  if (M < 0 || world <= 0 || rank < 0 || rank >= world || row0 == nullptr) return -1;
+  const int base = M / world, extra = M % world;
+  *row0 = rank * base + std::min(rank, extra);
+  return base + (rank < extra ? 1 : 0);
+}
+
+extern "C" GEMM_API int gemm_selftest_wait_timeout(int timeout_us, cudaStream_t stream) {
+  DeviceInfo& d = device_info();
+  if (timeout_us <= 0) timeout_us = 1;
+  log_launch("wait_probe_kernel", 0, 0, 0, dim3(1), dim3(32));
+  wait_probe_kernel<<<1, 32, 0, stream>>>(static_cast<unsigned long long>(timeout_us) * 1000ull,
+                                          d.err);
+  record_error(cudaGetLastError());
+  record_error(cudaStreamSynchronize(stream));
+  return gemm_launcher_status();
+}

@@ -1,0 +1,126 @@
+"""Python host side of the B200 FP16 GEMM library.
+
+The library is native: every computation runs in `lib/libgemm.so` (built from
+`csrc/` for sm_100a). This module only binds its C ABI with ctypes, the way the
+reference's own harness binds its `gemm_launcher` (tests/test_gemm.py:194-197:
+`argtypes = [c_void_p]*3 + [c_int]*3 + [c_float]*2`, `restype = None`), and
+adds torch-tensor conveniences on top. There is no fallback: if the shared
+library is missing or fails to load, `load()` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+PKG_ROOT = Path(__file__).resolve().parent.parent
+LIB_PATH = PKG_ROOT / "lib" / "libgemm.so"
+
+PATH_AUTO, PATH_TC, PATH_ROWS, PATH_COL = 0, 1, 2, 3
+
+_lib: ctypes.CDLL | None = None
+
+
+class GemmError(RuntimeError):
+    pass
+
+
+def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
+    vp, i, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    gemm8 = [vp, vp, vp, i, i, i, f, f]
+    lib.gemm_launcher.argtypes = gemm8
+    lib.gemm_launcher.restype = None
+    lib.gemm_launcher_stream.argtypes = gemm8 + [vp]
+    lib.gemm_launcher_stream.restype = None
+    lib.gemm_launcher_ex.argtypes = gemm8 + [vp, i, i]
+    lib.gemm_launcher_ex.restype = i
+    lib.gemm_launcher_status.argtypes = []
+    lib.gemm_launcher_status.restype = i
+    lib.gemm_last_kernel.argtypes = []
+    lib.gemm_last_kernel.restype = ctypes.c_char_p
+    lib.gemm_cublas.argtypes = gemm8
+    lib.gemm_cublas.restype = None
+    lib.gemm_cublas_stream.argtypes = gemm8 + [vp]
+    lib.gemm_cublas_stream.restype = None
+    lib.gemm_slab_rows.argtypes = [i, i, i, ctypes.POINTER(i)]
+    lib.gemm_slab_rows.restype = i
+    lib.gemm_selftest_wait_timeout.argtypes = [i, vp]
+    lib.gemm_selftest_wait_timeout.restype = i
+    return lib
+
+
+def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    """Load (once) and bind libgemm.so. Raises GemmError if it is absent."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        raise GemmError(f"{p} is missing: build it with `python gemm-project_b200/build.py`")
+    lib = _bind(ctypes.CDLL(str(p)))
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def _stream_handle(stream) -> int:
+    if stream is None:
+        import torch
+        stream = torch.cuda.current_stream()
+    return int(getattr(stream, "cuda_stream", stream))
+
+
+def _check(a, b, c):
+    import torch
+    for name, t in (("A", a), ("B", b), ("C", c)):
+        if t.dtype != torch.float16 or not t.is_cuda:
+            raise GemmError(f"{name} must be a CUDA float16 tensor")
+        if not t.is_contiguous():
+            raise GemmError(f"{name} must be contiguous row-major")
+    m, k = a.shape
+    k2, n = b.shape
+    if k2 != k or tuple(c.shape) != (m, n):
+        raise GemmError(f"shape mismatch A{tuple(a.shape)} B{tuple(b.shape)} C{tuple(c.shape)}")
+    return m, n, k
+
+
+def gemm(a, b, c, alpha: float = 1.0, beta: float = 0.0, stream=None, path: int = PATH_AUTO,
+         tile_n: int = 0) -> None:
+    """C = half(alpha * A@B (FP32 accumulate) + beta * C), in place, on `stream`
+    (torch's current stream by default). Asynchronous like the C entry point."""
+    lib = load()
+    m, n, k = _check(a, b, c)
+    s = _stream_handle(stream)
+    if path == PATH_AUTO and tile_n == 0:
+        lib.gemm_launcher_stream(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, alpha, beta, s)
+    else:
+        rc = lib.gemm_launcher_ex(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, alpha, beta, s,
+                                  path, tile_n)
+        if rc != 0:
+            raise GemmError(f"path {path} / tile_n {tile_n} cannot serve M={m} N={n} K={k}")
+
+
+def cublas(a, b, c, alpha: float = 1.0, beta: float = 0.0, stream=None) -> None:
+    """cuBLAS comparator with the same semantics (benchmarks only)."""
+    lib = load()
+    m, n, k = _check(a, b, c)
+    lib.gemm_cublas_stream(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, alpha, beta,
+                           _stream_handle(stream))
+
+
+def status() -> int:
+    """Sticky library status (0 = ok); see include/gemm_b200.h."""
+    return int(load().gemm_launcher_status())
+
+
+def last_kernel() -> str:
+    return load().gemm_last_kernel().decode()
+
+
+def slab_rows(m: int, world: int, rank: int) -> tuple[int, int]:
+    """(row0, rows) of the C row slab that `rank` of `world` owns."""
+    row0 = ctypes.c_int(0)
+    rows = load().gemm_slab_rows(m, world, rank, ctypes.byref(row0))
+    if rows < 0:
+        raise GemmError(f"invalid slab request M={m} world={world} rank={rank}")
+    return row0.value, rows

@@ -1,0 +1,98 @@
+/*
+ * B200 (sm_100a) FP16 GEMM library: C ABI.
+ *
+ * All matrices are contiguous row-major FP16 device buffers owned by the caller:
+ *   A[M,K], B[K,N], C[M,N];  C = half_rn(alpha * FP32acc(A*B) + beta * float(C)).
+ * C is not read when beta == 0 (a NaN-filled C gives a finite result).
+ * M <= 0 or N <= 0 is a no-op; K <= 0 gives C = half_rn(beta * C).
+ * Calls are asynchronous; the caller synchronizes before reading C.
+ */
+#ifndef GEMM_B200_H
+#define GEMM_B200_H
+
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+#include <cuda_fp16.h>
+typedef __half gemm_half_t;
+#else
+typedef unsigned short gemm_half_t; /* IEEE binary16 bit pattern */
+#endif
+
+#if defined(__GNUC__)
+#define GEMM_API __attribute__((visibility("default")))
+#else
+#define GEMM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Drop-in for the reference entry point, same signature and semantics:
+ * reference src/gemm.cu:104-105 (`extern "C" void gemm_launcher(const half*,
+ * const half*, half*, int M, int N, int K, float alpha, float beta)`), bound by
+ * ctypes in tests/test_gemm.py:194-197 with argtypes [c_void_p]*3 + [c_int]*3 +
+ * [c_float]*2 and restype None. Runs on the legacy default stream. Prints the
+ * reference's launch line ("Launching <kernel>: M=.. N=.. K=.., grid=(..),
+ * block=(..)", src/gemm.cu:12-16) unless GEMM_LAUNCH_LOG=0. */
+GEMM_API void gemm_launcher(const gemm_half_t* A, const gemm_half_t* B, gemm_half_t* C, int M, int N,
+                   int K, float alpha, float beta);
+
+/* Same as gemm_launcher on an explicit stream. Counterpart of the reference's
+ * stream-taking launcher samples/trtllm_gemm/launcher.cu:4-23
+ * (launchGemmSample(a, b, c, m, n, k, stream)), without its M <= 16 limit. */
+GEMM_API void gemm_launcher_stream(const gemm_half_t* A, const gemm_half_t* B, gemm_half_t* C, int M,
+                          int N, int K, float alpha, float beta, cudaStream_t stream);
+
+/* Kernel-path selection for tests and benchmarks (no counterpart in the
+ * reference, whose kernels are chosen only by src/gemm.cu:18-133).
+ * path: 0 = automatic (what gemm_launcher does), 1 = tcgen05 tile kernel,
+ * 2 = multi-row streaming kernel (M <= 8), 3 = column kernel (N == 1).
+ * tile_n: 0 = automatic, else 64, 128 or 256 for path 1.
+ * Returns 0, or -1 if the forced path cannot serve the shape. */
+GEMM_API int gemm_launcher_ex(const gemm_half_t* A, const gemm_half_t* B, gemm_half_t* C, int M, int N,
+                     int K, float alpha, float beta, cudaStream_t stream, int path, int tile_n);
+
+/* Sticky status of this library (no counterpart in the reference, which
+ * returns nothing and checks no launch, src/gemm.cu:104-134). Returns 0 when
+ * every call since the last query launched and no kernel reported an error,
+ * a cudaError_t value (1..999) for the first failed launch on this thread, or
+ * 1000 + code for a device-side bounded wait that ran out
+ * (1001 producer, 1002 MMA issuer, 1003 epilogue, 1005 wait probe).
+ * Reading the device word synchronizes with the legacy default stream.
+ * The status is cleared by the call. */
+GEMM_API int gemm_launcher_status(void);
+
+/* Name of the last kernel this thread launched through the library, in the
+ * launch-log spelling (the reference exposes it only through stdout,
+ * src/gemm.cu:12-16, parsed by tools/project.py:275-283). */
+GEMM_API const char* gemm_last_kernel(void);
+
+/* cuBLAS comparator: cublasGemmEx FP16 in/out, CUBLAS_COMPUTE_32F, row-major
+ * through C^T = B^T A^T, reduced-precision reductions disallowed. Replaces
+ * reference src/lib/gemm_cublas.cuh:38-63 with the 8 arguments its ctypes
+ * caller actually passes (tools/project.py:158-159); default stream. */
+GEMM_API void gemm_cublas(const gemm_half_t* A, const gemm_half_t* B, gemm_half_t* C, int M, int N, int K,
+                 float alpha, float beta);
+GEMM_API void gemm_cublas_stream(const gemm_half_t* A, const gemm_half_t* B, gemm_half_t* C, int M, int N,
+                        int K, float alpha, float beta, cudaStream_t stream);
+
+/* Row-slab partition used by the multi-GPU launcher (no counterpart in the
+ * reference, which is single-GPU): rank `rank` of `world` owns C rows
+ * [*row0, *row0 + return value); the first M % world ranks get one extra row.
+ * Returns -1 on invalid arguments. Pure host function. */
+GEMM_API int gemm_slab_rows(int M, int world, int rank, int* row0);
+
+/* Failure-detection self test (no counterpart in the reference): launches a
+ * one-CTA kernel that waits on an mbarrier nothing will complete, bounded by
+ * timeout_us microseconds. The kernel records code 5 in the device error word
+ * and returns instead of hanging; the call synchronizes the stream and returns
+ * gemm_launcher_status() (1005 when the bound worked). */
+GEMM_API int gemm_selftest_wait_timeout(int timeout_us, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GEMM_B200_H */

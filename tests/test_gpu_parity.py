@@ -1,0 +1,190 @@
+"""Parity of the CUDA library with the CPU oracle, through the C ABI (needs a B200).
+
+Coverage follows the reference's suite (tests/test_gemm.py): its launcher
+cases by class (LLM projection shapes at decode/prefill token counts, odd M,
+K = 1025, K = 0, M = 0, N = 0), its misaligned A/B/C cases, its exact
+known-answer cases, canaries and NaN-filled C, plus every BASELINE config and
+every kernel path forced on shapes that cross its tile edges.
+"""
+import ctypes
+
+import pytest
+import torch
+
+from gpu_harness import Guarded, run, verify
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+PATH_TC, PATH_ROWS, PATH_COL = 1, 2, 3
+
+
+def _go(lib, cuda, m, n, k, alpha=1.0, beta=0.0, **kw):
+    c, a, b, c0 = run(lib, cuda, m, n, k, alpha, beta, **kw)
+    chk = verify(c, a, b, c0, alpha, beta, seed=kw.get("seed", 0))
+    assert chk.passed, f"{(m, n, k)} alpha={alpha} beta={beta} {kw}: {chk}"
+    return chk
+
+
+# ---------------------------------------------------------------------------
+# BASELINE.json configs
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("name", ["square1024", "square4096", "square8192", "gemv_m1", "gemv_n1",
+                                  "odd_1023", "odd_3"])
+def test_baseline_config(lib, cuda, name):
+    cfg = oracle.CONFIGS[name]
+    off = cfg.get("offset", 0)
+    _go(lib, cuda, cfg["m"], cfg["n"], cfg["k"], cfg["alpha"], cfg["beta"], dist=cfg["dist"],
+        offsets=(off, off, off), fn="launcher")
+
+
+def test_sharded_config_one_slab(lib, cuda):
+    """One 4096-row slab of the 32768x32768x16384 config (what each of 8 ranks runs)."""
+    _go(lib, cuda, 4096, 32768, 16384, 1.0, 0.0, dist="normal", fn="launcher")
+
+
+# ---------------------------------------------------------------------------
+# Every path, forced, across tile and K-block edges
+# ---------------------------------------------------------------------------
+TC_SHAPES = [(128, 256, 64), (256, 512, 128), (129, 257, 65), (1, 8, 8), (127, 200, 1000),
+             (300, 1000, 72), (1024, 1024, 1024), (640, 384, 4104), (2048, 2048, 64)]
+
+
+@pytest.mark.parametrize("tile_n", [64, 128, 256])
+@pytest.mark.parametrize("shape", TC_SHAPES, ids=str)
+def test_tc_path(lib, cuda, shape, tile_n):
+    m, n, k = shape
+    _go(lib, cuda, m, n, k, 0.75, 0.5, dist="normal", path=PATH_TC, tile_n=tile_n, seed=m + n + k)
+
+
+@pytest.mark.parametrize("shape", [(1, 8, 8), (2, 264, 300), (3, 5000, 4097), (4, 1024, 1025),
+                                   (5, 2048, 8192), (8, 6144, 4096), (1, 28672, 8192),
+                                   (7, 131, 515), (1, 1, 9), (6, 24, 20000)], ids=str)
+@pytest.mark.parametrize("offset", [0, 1, 3])
+def test_rows_path(lib, cuda, shape, offset):
+    m, n, k = shape
+    _go(lib, cuda, m, n, k, 0.7, -0.3, path=PATH_ROWS, offsets=(offset, offset, offset),
+        seed=m * 31 + offset)
+
+
+@pytest.mark.parametrize("shape", [(28672, 1, 8192), (9, 1, 8), (1000, 1, 777), (4096, 1, 14336),
+                                   (33, 1, 1)], ids=str)
+@pytest.mark.parametrize("offset", [0, 1])
+def test_col_path(lib, cuda, shape, offset):
+    m, n, k = shape
+    _go(lib, cuda, m, n, k, 1.0, 0.25, path=PATH_COL, offsets=(offset, offset, offset), seed=m)
+
+
+# ---------------------------------------------------------------------------
+# The reference's launcher cases by class (tests/test_gemm.py:12-23,107-163)
+# ---------------------------------------------------------------------------
+MODEL_DIMS = {"llama3_8b": (4096, 14336, 1024, 128256), "qwen25_7b": (3584, 18944, 512, 152064)}
+
+
+def _llm_cases():
+    cases = [(1024, 1024, 1024)]
+    for hidden, ffn, kv, vocab in MODEL_DIMS.values():
+        for n, k in [(hidden + 2 * kv, hidden), (hidden, hidden), (2 * ffn, hidden), (hidden, ffn)]:
+            for m in [1, 8, 32, 64, 128, 512, 2048]:
+                cases.append((m, n, k))
+        for m in [1, 32, 128]:
+            cases.append((m, vocab, hidden))
+    return cases
+
+
+@pytest.mark.parametrize("shape", _llm_cases(), ids=str)
+def test_llm_projection_shapes(lib, cuda, shape):
+    m, n, k = shape
+    c, a, b, c0 = run(lib, cuda, m, n, k, 1.0, 0.0, dist="normal", seed=sum(shape), fn="launcher")
+    chk = verify(c, a, b, c0, 1.0, 0.0, sample_rows=64)
+    assert chk.passed, f"{shape}: {chk}"
+
+
+REGRESSION = [(1, 4096, 1025), (1, 512, 1025), (1, 1024, 8192), (2, 512, 512), (3, 576, 640),
+              (17, 640, 672), (31, 512, 1024), (47, 1024, 512), (63, 1024, 640), (65, 1024, 640),
+              (96, 1024, 1024), (128, 576, 18944), (384, 2048, 14336), (1664, 2048, 14336),
+              (832, 2048, 8256), (17, 19, 0)]
+
+
+@pytest.mark.parametrize("shape", REGRESSION, ids=str)
+def test_regression_shapes(lib, cuda, shape):
+    m, n, k = shape
+    c, a, b, c0 = run(lib, cuda, m, n, k, 0.7, -0.3, seed=m + k, c_init=2.0, fn="launcher")
+    chk = verify(c, a, b, c0, 0.7, -0.3)
+    assert chk.passed, f"{shape}: {chk}"
+
+
+@pytest.mark.parametrize("m,n", [(0, 19), (19, 0), (0, 0)])
+def test_empty_output_is_noop(lib, cuda, m, n):
+    gc = Guarded((max(m, 1), max(n, 1)), cuda, fill=7.0)
+    a = torch.ones(64, device=cuda, dtype=torch.float16)
+    torch.cuda.synchronize()
+    lib.gemm_launcher(a.data_ptr(), a.data_ptr(), gc.tensor.data_ptr(), m, n, 32,
+                      ctypes.c_float(1.0), ctypes.c_float(1.0))
+    torch.cuda.synchronize()
+    assert lib.gemm_launcher_status() == 0
+    assert bool((gc.tensor == 7.0).all()) and gc.canaries_ok()
+
+
+@pytest.mark.parametrize("beta", [0.0, -0.5])
+def test_k_zero_scales_c(lib, cuda, beta):
+    c, a, b, c0 = run(lib, cuda, 17, 19, 0, 1.0, beta, fn="launcher")
+    expect = torch.zeros(17, 19) if beta == 0.0 else (beta * c0.float())
+    assert torch.equal(c.cpu(), expect.half())
+
+
+@pytest.mark.parametrize("which", ["A", "B", "C"])
+def test_single_pointer_misaligned(lib, cuda, which):
+    """One pointer shifted by one half (tests/test_gemm.py:140-162)."""
+    off = {"A": (1, 0, 0), "B": (0, 1, 0), "C": (0, 0, 1)}[which]
+    c, a, b, c0 = run(lib, cuda, 17, 1024, 544, 0.7, -0.3, offsets=off, c_init=2.0, fn="launcher")
+    assert verify(c, a, b, c0, 0.7, -0.3).passed
+    c, a, b, c0 = run(lib, cuda, 300, 1024, 544, 0.7, -0.3, offsets=off, c_init=2.0, fn="launcher")
+    assert verify(c, a, b, c0, 0.7, -0.3).passed
+
+
+# ---------------------------------------------------------------------------
+# Exact known-answer cases (tests/test_gemm.py:166-184)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("m,n,k,tiny", [(1, 4096, 18944, False), (8, 1024, 18944, False),
+                                        (32, 1024, 4096, True), (256, 6144, 4096, False),
+                                        (256, 2048, 18944, False), (4096, 1, 18944, False)])
+def test_exact_known_answers(lib, cuda, m, n, k, tiny):
+    ga = Guarded((m, k), cuda, fill=2.0 ** -13 if tiny else 256.0)
+    gb = Guarded((k, n), cuda, fill=2.0 ** -13 if tiny else 1.0)
+    if not tiny:
+        if n == 1:
+            ga.tensor[:, k // 2:] = -256.0
+            ga.tensor[:, -1] = -224.0
+        else:
+            gb.tensor[k // 2:] = -1.0
+            gb.tensor[-1] = -0.875
+    gc = Guarded((m, n), cuda)
+    torch.cuda.synchronize()
+    lib.gemm_launcher(ga.tensor.data_ptr(), gb.tensor.data_ptr(), gc.tensor.data_ptr(), m, n, k,
+                      ctypes.c_float(1.0), ctypes.c_float(0.0))
+    torch.cuda.synchronize()
+    expected = k * 2.0 ** -26 if tiny else 32.0
+    assert lib.gemm_launcher_status() == 0
+    assert bool((gc.tensor == expected).all()), f"{(m, n, k)} not exact"
+    assert gc.canaries_ok()
+
+
+def test_cublas_comparator_agrees(lib, cuda):
+    c, a, b, c0 = run(lib, cuda, 512, 768, 1024, 0.5, 0.5, fn="cublas")
+    assert verify(c, a, b, c0, 0.5, 0.5).passed
+
+
+def test_dispatch_choices(lib, cuda):
+    """The automatic dispatch picks the sm_100a kernel family for each config class."""
+    import gemm_b200
+    names = {}
+    for shape in [(1024, 1024, 1024), (1, 28672, 8192), (28672, 1, 8192), (3, 5000, 4097),
+                  (8192, 8192, 64)]:
+        run(lib, cuda, *shape, fn="launcher")
+        names[shape] = gemm_b200.last_kernel()
+    assert names[(1024, 1024, 1024)].startswith("tc_gemm_kernel")
+    assert names[(8192, 8192, 64)].startswith("tc_gemm_kernel<128x256>")
+    assert names[(1, 28672, 8192)].startswith("rows_gemv_kernel<1>")
+    assert names[(28672, 1, 8192)].startswith("col_gemv_kernel")
+    assert names[(3, 5000, 4097)].startswith("rows_gemv_kernel<4>")
