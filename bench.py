@@ -1,0 +1,523 @@
+"""Benchmark of the B200 FP16 GEMM library (one JSON line on rank 0).
+
+Workloads:
+  N = 1   : square FP16 GEMM 8192^3, A,B ~ N(0,1/sqrt(K)), C ~ U[-1,1), alpha 1, beta 0.5
+            (the config the headline TFLOP/s metric is quoted on). The same line
+            carries the other single-GPU configs under "configs": the M=1 and N=1
+            GEMVs (GB/s), 4096^3, 1024^3 and the odd/misaligned shapes, each next to
+            cuBLAS on the same inputs.
+  N > 1   : the sharded 32768 x 32768 x 16384 GEMM, weak-scaled: every rank owns a
+            4096-row C slab (4096 x 32768 x 16384 per rank, the 8-GPU partition of
+            the config); B is generated on rank 0 and broadcast once over NCCL
+            (timed separately, outside the steps); no collective inside a step.
+A step is one gemm_launcher call over the workload. Inputs are larger than the
+126 MB L2 (no flush needed). Times are CUDA events on the launching stream,
+max over ranks.
+
+`--impl reference` times the reference's CPU path for the same config on the host
+cores: its tests' check formula alpha*(A.float()@B.float()) + beta*C.float()
+(tests/test_gemm.py:91,130,156) in torch FP32 on the CPU, each step a bounded
+sample of rows of the same GEMM.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+PKG = REPO / "gemm-project_b200"
+sys.path.insert(0, str(PKG))
+os.environ.setdefault("GEMM_LAUNCH_LOG", "0")
+
+L2_BYTES = 126 * 1024 * 1024
+METRIC = "FP16 GEMM TFLOP/s (% dense peak) at 8192³; M=1 GEMV GB/s vs HBM peak"
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "tflops": d["bf16_tflops"],
+                "tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+def dev_inputs(m, n, k, dist, c_dist, seed, device):
+    """Seeded device-resident inputs (drawn on the GPU: the full configs are too
+    large to draw on the CPU inside a short benchmark)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    if dist == "normal":
+        a = (torch.randn((m, k), generator=g, device=device) / math.sqrt(k)).half()
+        b = (torch.randn((k, n), generator=g, device=device) / math.sqrt(k)).half()
+    else:
+        a = (torch.rand((m, k), generator=g, device=device) * 2 - 1).half()
+        b = (torch.rand((k, n), generator=g, device=device) * 2 - 1).half()
+    if c_dist == "zero":
+        c = torch.zeros((m, n), device=device, dtype=torch.float16)
+    else:
+        c = (torch.rand((m, n), generator=g, device=device) * 2 - 1).half()
+    return a, b, c
+
+
+def offset_copy(t, off):
+    """Same values, base pointer shifted by `off` halves inside a larger allocation."""
+    if off == 0:
+        return t
+    buf = torch.empty(t.numel() + off, dtype=t.dtype, device=t.device)
+    v = buf[off:].view(t.shape)
+    v.copy_(t)
+    return v
+
+
+def time_calls(fn, steps, warmup, stream):
+    """Average ms per call over `steps` back-to-back calls (CUDA events on `stream`)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps
+
+
+def traffic_from_profile(name: str):
+    """dram bytes per launch recorded from an ncu capture in profiles/<name>.txt
+    (line `dram_bytes_per_launch: <int>`), else None."""
+    p = REPO / "profiles" / f"{name}.txt"
+    if not p.exists():
+        return None
+    for ln in p.read_text().splitlines():
+        if ln.startswith("dram_bytes_per_launch:"):
+            try:
+                return int(float(ln.split(":", 1)[1].strip().split()[0]))
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_reference_rate(m, n, k, dist, alpha, beta, budget_s=8.0, threads=None):
+    """Time the reference's CPU check formula on a bounded row sample of the
+    same GEMM; returns (TFLOP/s, rows, seconds, threads)."""
+    sys.path.insert(0, str(REPO))
+    from oracle import oracle
+    threads = threads or oracle.cpu_threads()
+    torch.set_num_threads(threads)
+    rows = min(m, 256)
+    a, b, c = oracle.make_inputs(rows, n, k, dist, seed=0)
+    oracle.reference_fp32(a, b, c, alpha, beta)  # warm up BLAS
+    t0 = time.perf_counter()
+    oracle.reference_fp32(a, b, c, alpha, beta)
+    dt = time.perf_counter() - t0
+    # grow the sample to about budget_s of CPU work
+    target_rows = int(min(m, max(rows, rows * budget_s / max(dt, 1e-6) / 2)))
+    if target_rows > rows:
+        a, b, c = oracle.make_inputs(target_rows, n, k, dist, seed=0)
+        rows = target_rows
+    reps, total = 0, 0.0
+    while total < budget_s / 2 or reps < 1:
+        t0 = time.perf_counter()
+        oracle.reference_fp32(a, b, c, alpha, beta)
+        total += time.perf_counter() - t0
+        reps += 1
+    tflops = 2.0 * rows * n * k * reps / total / 1e12
+    return tflops, rows, total, threads
+
+
+# ---------------------------------------------------------------------------
+# single-GPU workloads
+# ---------------------------------------------------------------------------
+def measure_config(gb, name, cfg, stream, steps, warmup, device):
+    m, n, k = cfg["m"], cfg["n"], cfg["k"]
+    a, b, c = dev_inputs(m, n, k, cfg["dist"], cfg.get("c_dist", "uniform"), 0, device)
+    off = cfg.get("offset", 0)
+    a, b, c = offset_copy(a, off), offset_copy(b, off), offset_copy(c, off)
+    alpha, beta = cfg["alpha"], cfg["beta"]
+    c_ours = c.clone() if off == 0 else offset_copy(c, off)
+    c_cub = c.clone()
+    ms = time_calls(lambda: gb.gemm(a, b, c_ours, alpha, beta, stream), steps, warmup, stream)
+    kernel = gb.last_kernel()
+    ms_cub = time_calls(lambda: gb.cublas(a, b, c_cub, alpha, beta, stream), steps, warmup, stream)
+    flops = 2.0 * m * n * k
+    bytes_ = 2.0 * (m * k + k * n + m * n) + (2.0 * m * n if beta != 0 else 0.0)
+    return {"M": m, "N": n, "K": k, "kernel": kernel, "us": ms * 1e3, "cublas_us": ms_cub * 1e3,
+            "tflops": flops / ms / 1e9, "gbs": bytes_ / ms / 1e6,
+            "cublas_tflops": flops / ms_cub / 1e9, "cublas_gbs": bytes_ / ms_cub / 1e6,
+            "vs_cublas": ms_cub / ms}
+
+
+def run_single(args, gb, oracle_cfgs, device, pk):
+    stream = torch.cuda.current_stream()
+    cfg = oracle_cfgs["square8192"]
+    m, n, k, alpha, beta = cfg["m"], cfg["n"], cfg["k"], cfg["alpha"], cfg["beta"]
+    a, b, c = dev_inputs(m, n, k, "normal", "uniform", 0, device)
+    flops = 2.0 * m * n * k
+    steps, warmup = args.steps, max(args.warmup, 3)
+    # warm-up (untimed)
+    for _ in range(warmup):
+        gb.gemm(a, b, c, alpha, beta, stream)
+    torch.cuda.synchronize()
+    kernel = gb.last_kernel()
+    with ClockSampler(device.index) as clk:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(steps):
+            gb.gemm(a, b, c, alpha, beta, stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+        time.sleep(0.25)
+    ms = start.elapsed_time(end) / steps
+    st = gb.status()
+    if st != 0:
+        raise RuntimeError(f"library status {st} during the timed region")
+    value = flops / ms / 1e9  # TFLOP/s
+
+    # e2e through the public API: pinned host inputs -> device, GEMM, C -> host
+    a_h = a.cpu().pin_memory()
+    b_h = b.cpu().pin_memory()
+    c_h = c.cpu().pin_memory()
+    c_out = torch.empty_like(c_h).pin_memory()
+    a_d, b_d, c_d = torch.empty_like(a), torch.empty_like(b), torch.empty_like(c)
+
+    def e2e_step():
+        a_d.copy_(a_h, non_blocking=True)
+        b_d.copy_(b_h, non_blocking=True)
+        c_d.copy_(c_h, non_blocking=True)
+        gb.gemm(a_d, b_d, c_d, alpha, beta, stream)
+        c_out.copy_(c_d, non_blocking=True)
+
+    e2e_steps = max(3, min(steps, 10))
+    e2e_ms = time_calls(e2e_step, e2e_steps, 2, stream)
+    h2d = (a.numel() + b.numel() + c.numel()) * 2
+    d2h = c.numel() * 2
+
+    ms_cub = time_calls(lambda: gb.cublas(a, b, c, alpha, beta, stream), steps, warmup, stream)
+
+    # other single-GPU configs (each next to cuBLAS on the same inputs)
+    configs = {}
+    if not args.quick:
+        for name in ["square4096", "square1024", "gemv_m1", "gemv_n1", "odd_1023", "odd_3"]:
+            reps = 20 if name != "square4096" else 10
+            configs[name] = measure_config(gb, name, oracle_cfgs[name], stream, reps, 5, device)
+        # the per-rank slab of the sharded config on one GPU, for the scaling comparison
+        sl = dict(oracle_cfgs["sharded32768"], m=4096)
+        configs["slab4096x32768x16384"] = measure_config(gb, "slab", sl, stream, 3, 2, device)
+        for key in ("gemv_m1", "gemv_n1"):
+            configs[key]["hbm_frac"] = configs[key]["gbs"] / pk["hbm_gbs"]
+            configs[key]["hbm_frac_unit"] = f"of {pk['source']} {pk['hbm_gbs']} GB/s copy"
+
+    traffic = traffic_from_profile("tc_gemm_8192")
+    tflop_peak = pk["tflops"]
+    roof = {"bound": "tensor", "achieved": value, "peak": tflop_peak, "unit": "TFLOP/s",
+            "frac": value / tflop_peak, "traffic": traffic,
+            "kernel": kernel, "peak_source": f"{pk['source']} cuBLAS bf16 burst",
+            "algorithmic_flop_per_launch": flops,
+            "frac_of_nominal_2250": value / 2250.0}
+    tflops_cpu, rows, secs, threads = cpu_reference_rate(m, n, k, "normal", alpha, beta,
+                                                          budget_s=args.cpu_budget)
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": steps, "warmup": warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 in, fp32 accumulate",
+        "data": "synthetic (seeded on device: A,B ~ N(0,1/sqrt(K)), C ~ U[-1,1))",
+        "config": {"workload": "square FP16 GEMM M=N=K=8192, alpha=1, beta=0.5 (BASELINE configs[1])",
+                   "M": m, "N": n, "K": k, "alpha": alpha, "beta": beta, "parallelism": "1 GPU",
+                   "l2": "inputs (384 MiB) larger than the 126 MB L2; no flush"},
+        "roofline": roof,
+        "cublas": {"tflops": round(flops / ms_cub / 1e9, 2), "ms": round(ms_cub, 4),
+                   "ours_vs_cublas": round(ms_cub / ms, 4)},
+        "e2e": {"value": round(flops / e2e_ms / 1e9, 3), "unit": "TFLOP/s",
+                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "api": "gemm_launcher_stream via ctypes, pinned host buffers"},
+        "cpu_baseline": {"value": round(tflops_cpu, 4), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port",
+                         "sample": f"torch CPU FP32 alpha*(A@B)+beta*C on {rows} of {m} rows "
+                                   f"(K={k}, N={n}), {secs:.1f} s"},
+        "gpu_launches": steps,
+        "clocks": clk.summary(),
+        "configs": configs,
+    }
+    return out
+
+
+# ---------------------------------------------------------------------------
+# multi-GPU slab workload (weak scaling)
+# ---------------------------------------------------------------------------
+def run_multi(args, gb, oracle_cfgs, device, pk, rank, world):
+    import torch.distributed as dist
+    cfg = oracle_cfgs["sharded32768"]
+    slab_m = cfg["m"] // 8  # 4096 rows per rank: the 8-GPU partition of the config
+    m_total = slab_m * world
+    n, k, alpha, beta = cfg["n"], cfg["k"], cfg["alpha"], cfg["beta"]
+    stream = torch.cuda.current_stream()
+    # B from rank 0, broadcast once over NCCL (timed on the device, max over ranks)
+    if rank == 0:
+        g = torch.Generator(device=device).manual_seed(0)
+        b = (torch.randn((k, n), generator=g, device=device) / math.sqrt(k)).half()
+    else:
+        b = torch.empty((k, n), device=device, dtype=torch.float16)
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    dist.broadcast(b, src=0)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    bcast_ms = torch.tensor([ev0.elapsed_time(ev1)], device=device)
+    dist.all_reduce(bcast_ms, op=dist.ReduceOp.MAX)
+    # this rank's A slab (seed = rank) and C slab (zero)
+    g = torch.Generator(device=device).manual_seed(1 + rank)
+    a = (torch.randn((slab_m, k), generator=g, device=device) / math.sqrt(k)).half()
+    c = torch.zeros((slab_m, n), device=device, dtype=torch.float16)
+    warmup = max(args.warmup, 3)
+    for _ in range(warmup):
+        gb.gemm(a, b, c, alpha, beta, stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    with ClockSampler(device.index) as clk:
+        torch.cuda.synchronize()
+        dist.barrier()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            gb.gemm(a, b, c, alpha, beta, stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        time.sleep(0.25)
+    ms = torch.tensor([start.elapsed_time(end) / args.steps], device=device)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    st = gb.status()
+    if st != 0:
+        raise RuntimeError(f"rank {rank}: library status {st}")
+    ms_v = float(ms.item())
+    flops_total = 2.0 * m_total * n * k
+    value = flops_total / ms_v / 1e9
+    # e2e per rank: this rank's A slab and C slab cross PCIe each step (B stays resident:
+    # it is replicated once by the broadcast, per the config)
+    a_h, c_h = a.cpu().pin_memory(), c.cpu().pin_memory()
+    c_out = torch.empty_like(c_h).pin_memory()
+    a_d, c_d = torch.empty_like(a), torch.empty_like(c)
+
+    def e2e_step():
+        a_d.copy_(a_h, non_blocking=True)
+        c_d.copy_(c_h, non_blocking=True)
+        gb.gemm(a_d, b, c_d, alpha, beta, stream)
+        c_out.copy_(c_d, non_blocking=True)
+
+    dist.barrier()
+    e2e = torch.tensor([time_calls(e2e_step, 3, 1, stream)], device=device)
+    dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e.item())
+    per_gpu = value / world
+    if rank != 0:
+        return None
+    return {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": warmup, "ms_per_step": round(ms_v, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp16 in, fp32 accumulate",
+        "data": "synthetic (seeded on device: A,B ~ N(0,1/sqrt(K)), C = 0)",
+        "config": {"workload": "sharded FP16 GEMM, 4096-row C slab per rank of the "
+                               "32768x32768x16384 config (BASELINE configs[4]); M = 4096 x n_gpus",
+                   "M": m_total, "N": n, "K": k, "alpha": alpha, "beta": beta,
+                   "parallelism": f"C row slabs x{world}, B broadcast once (NCCL)",
+                   "l2": "inputs larger than the 126 MB L2; no flush"},
+        "roofline": {"bound": "tensor", "achieved": round(per_gpu, 2), "peak": pk["tflops"],
+                     "unit": "TFLOP/s", "frac": per_gpu / pk["tflops"],
+                     "traffic": traffic_from_profile("tc_gemm_8192"),
+                     "peak_source": f"{pk['source']} cuBLAS bf16 burst, per GPU"},
+        "broadcast": {"bytes": k * n * 2, "ms_max_over_ranks": round(float(bcast_ms.item()), 3),
+                      "gbs": round(k * n * 2 / float(bcast_ms.item()) / 1e6, 1)},
+        "e2e": {"value": round(flops_total / e2e_ms / 1e9, 3), "unit": "TFLOP/s",
+                "ms_per_step": round(e2e_ms, 3),
+                "h2d_bytes_per_step": (a.numel() + c.numel()) * 2 * world,
+                "d2h_bytes_per_step": c.numel() * 2 * world},
+        "gpu_launches": args.steps * world,
+        "clocks": clk.summary(),
+    }
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's CPU check path on the host cores
+# ---------------------------------------------------------------------------
+def run_reference(args, oracle_cfgs, rank, world):
+    if rank != 0:
+        return None
+    sys.path.insert(0, str(REPO))
+    from oracle import oracle
+    if world > 1:
+        cfg = dict(oracle_cfgs["sharded32768"])
+        workload = ("sharded FP16 GEMM, 4096-row C slab per rank of the 32768x32768x16384 config; "
+                    "M = 4096 x n_gpus")
+        m = 4096 * world
+    else:
+        cfg = oracle_cfgs["square8192"]
+        workload = "square FP16 GEMM M=N=K=8192, alpha=1, beta=0.5 (BASELINE configs[1])"
+        m = cfg["m"]
+    n, k, alpha, beta = cfg["n"], cfg["k"], cfg["alpha"], cfg["beta"]
+    threads = oracle.cpu_threads()
+    torch.set_num_threads(threads)
+    # rows per step: a bounded sample so the whole run ends within minutes
+    rows = 64
+    a, b, c = oracle.make_inputs(rows, n, k, cfg["dist"], seed=0)
+    oracle.reference_fp32(a, b, c, alpha, beta)
+    t0 = time.perf_counter()
+    oracle.reference_fp32(a, b, c, alpha, beta)
+    dt = max(time.perf_counter() - t0, 1e-6)
+    per_step_budget = max(0.5, min(10.0, 60.0 / max(args.steps + args.warmup, 1)))
+    rows = int(max(64, min(m, rows * per_step_budget / dt)))
+    a, b, c = oracle.make_inputs(rows, n, k, cfg["dist"], seed=0)
+    for _ in range(max(args.warmup, 1)):
+        oracle.reference_fp32(a, b, c, alpha, beta)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.reference_fp32(a, b, c, alpha, beta)
+    secs = time.perf_counter() - t0
+    ms = secs / args.steps * 1e3
+    value = 2.0 * rows * n * k / (ms * 1e-3) / 1e12
+    sample = (f"torch CPU FP32 alpha*(A@B)+beta*C (the reference tests' check formula) on {rows} "
+              f"of {m} rows per step, K={k}, N={n}")
+    return {
+        "metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp16 in, fp32 accumulate (CPU)", "data": "synthetic (seeded CPU generator)",
+        "config": {"workload": workload, "M": m, "N": n, "K": k, "alpha": alpha, "beta": beta,
+                   "parallelism": "host CPU cores"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--quick", action="store_true", help="skip the secondary configs")
+    ap.add_argument("--cpu-budget", type=float, default=8.0, help="seconds of CPU baseline work")
+    ap.add_argument("--only", default=None,
+                    help="time one config of oracle.CONFIGS (ours and cuBLAS) and exit")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    sys.path.insert(0, str(REPO))
+    from oracle.oracle import CONFIGS  # config table only (shapes, distributions)
+
+    if args.impl == "reference":
+        # rank 0 alone times the CPU path; other ranks exit without work
+        out = run_reference(args, CONFIGS, rank, world)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
+
+    import gemm_b200 as gb
+    gb.load()  # raises if the CUDA library is missing: there is no fallback
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pk = peaks()
+    if args.only:
+        # profiling / sweep helper: one config, W + K launches, no baselines
+        cfg = dict(CONFIGS[args.only])
+        if args.only == "sharded32768":
+            cfg["m"] = 4096
+        r = measure_config(gb, args.only, cfg, torch.cuda.current_stream(), args.steps,
+                           args.warmup, device)
+        print(json.dumps({"only": args.only, **r}), flush=True)
+        return
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        out = run_multi(args, gb, CONFIGS, device, pk, rank, world)
+        dist.barrier()
+        dist.destroy_process_group()
+    else:
+        out = run_single(args, gb, CONFIGS, device, pk)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()
