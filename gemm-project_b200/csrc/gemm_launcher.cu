@@ -391,6 +391,128 @@ int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float a
   }
 }
 
+// ---------------------------------------------------------------------------
+// Repack path without allocation, for gemm_launcher_noalloc.
+//
+// The repack of a TMA-unaddressable A or B normally takes stream-ordered
+// scratch from cudaMallocAsync. Callers that cannot let a library allocate
+// device memory get this variant instead: the scratch is one file-scope
+// __device__ array of fixed size that every GPU loading the library holds
+// until the process exits. Its device address is looked up once per device
+// (cudaGetSymbolAddress, with that device current); host code never passes the
+// symbol itself to a kernel, since on the host it only names a stand-in.
+// Every call shares the array: calls that overlap on the GPU (different
+// streams, or different host threads) race on it. Nothing in it needs to start
+// at zero: the tensor maps declare only the real K and N extents and TMA
+// zero-fills everything beyond them, so the previous call's bytes are never read.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB per GPU
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocScratch {
+  void* ptr = nullptr;
+  bool ready = false;
+};
+NoAllocScratch g_noalloc[kMaxDevices];
+std::mutex g_noalloc_mutex;
+
+// Device address of g_noalloc_scratch on the current device; nullptr (with the
+// CUDA error recorded in the status) if it cannot be obtained.
+void* noalloc_scratch_ptr() {
+  int dev = 0;
+  const cudaError_t ge = cudaGetDevice(&dev);
+  if (ge != cudaSuccess) {
+    record_error(ge);
+    return nullptr;
+  }
+  NoAllocScratch& s = g_noalloc[dev % kMaxDevices];
+  if (s.ready) return s.ptr;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!s.ready) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      record_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+      return nullptr;
+    }
+    s.ptr = p;
+    s.ready = true;
+  }
+  return s.ptr;
+}
+
+// Bytes of repack scratch the tcgen05 path needs for these operands (0 when
+// both are TMA-addressable as they are). A's share is rounded up to 256 bytes
+// so that B's copy starts aligned.
+size_t repack_bytes(const half* A, const half* B, int M, int N, int K) {
+  size_t a_bytes = 0, b_bytes = 0;
+  if (!(aligned16(A) && K % 8 == 0)) a_bytes = static_cast<size_t>(M) * round_up8(K) * sizeof(half);
+  if (!(aligned16(B) && N % 8 == 0)) b_bytes = static_cast<size_t>(K) * round_up8(N) * sizeof(half);
+  return (a_bytes + 255) / 256 * 256 + b_bytes;
+}
+
+// The repack + tcgen05 path with caller-provided scratch (no allocation).
+int launch_tc_static_scratch(const half* A, const half* B, half* C, int M, int N, int K,
+                             float alpha, float beta, cudaStream_t s, const DeviceInfo& d,
+                             void* scratch) {
+  const bool a_ok = aligned16(A) && K % 8 == 0;
+  const bool b_ok = aligned16(B) && N % 8 == 0;
+  const half* a_src = A;
+  const half* b_src = B;
+  int lda = K, ldb = N;
+  size_t a_bytes = a_ok ? 0 : static_cast<size_t>(M) * round_up8(K) * sizeof(half);
+  a_bytes = (a_bytes + 255) / 256 * 256;
+  const int threads = 256;
+  if (!a_ok) {
+    lda = round_up8(K);
+    half* dst = static_cast<half*>(scratch);
+    const size_t work = static_cast<size_t>(M) * ceil_div(K, 8);
+    const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
+    log_launch("pack_rows_kernel<A,static>", M, N, K, dim3(blocks), dim3(threads));
+    pack_rows_kernel<<<blocks, threads, 0, s>>>(A, K, dst, lda, M, K);
+    record_error(cudaGetLastError());
+    a_src = dst;
+  }
+  if (!b_ok) {
+    ldb = round_up8(N);
+    half* dst = reinterpret_cast<half*>(static_cast<char*>(scratch) + a_bytes);
+    const size_t work = static_cast<size_t>(K) * ceil_div(N, 8);
+    const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
+    log_launch("pack_rows_kernel<B,static>", M, N, K, dim3(blocks), dim3(threads));
+    pack_rows_kernel<<<blocks, threads, 0, s>>>(B, N, dst, ldb, K, N);
+    record_error(cudaGetLastError());
+    b_src = dst;
+  }
+  const int bn = choose_tile_n(M, N, d.sms);
+  CUtensorMap ta, tb;
+  if (!(make_tmap(&ta, a_src, K, M, static_cast<uint64_t>(lda) * 2, 64, 128) &&
+        make_tmap(&tb, b_src, N, K, static_cast<uint64_t>(ldb) * 2, 64, 64))) {
+    record_error(cudaErrorInvalidValue);
+    return -1;
+  }
+  TcParams p{};
+  p.C = C;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = N;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.tiles_m = ceil_div(M, 128);
+  p.tiles_n = ceil_div(N, bn);
+  p.num_kb = ceil_div(K, 64);
+  p.group = std::min(p.tiles_m, 8);
+  p.c_vec_ok = aligned16(C) && N % 8 == 0;
+  p.timeout_ns = wait_timeout_ns();
+  p.err = d.err;
+  switch (bn) {
+    case 64: launch_tc_bn<64>(ta, tb, p, d.sms, s, M, N, K); break;
+    case 128: launch_tc_bn<128>(ta, tb, p, d.sms, s, M, N, K); break;
+    default: launch_tc_bn<256>(ta, tb, p, d.sms, s, M, N, K); break;
+  }
+  return 0;
+}
+
 }  // namespace
 }  // namespace gemm_b200
 
@@ -431,6 +553,28 @@ extern "C" GEMM_API int gemm_slab_rows(int M, int world, int rank, int* row0) {
   const int base = M / world, extra = M % world;
   *row0 = rank * base + std::min(rank, extra);
   return base + (rank < extra ? 1 : 0);
+}
+
+extern "C" GEMM_API int gemm_launcher_noalloc(const half* A, const half* B, half* C, int M, int N,
+                                              int K, float alpha, float beta, cudaStream_t stream) {
+  if (M <= 0 || N <= 0) return 0;
+  const bool tc_path = K > 0 && M > 8 && N != 1;  // the choice dispatch() makes
+  const size_t need = tc_path ? repack_bytes(A, B, M, N, K) : 0;
+  if (need == 0) {
+    // No repack: the kernels dispatch() picks here allocate nothing.
+    return dispatch(A, B, C, M, N, K, alpha, beta, stream, 0, 0) == 0 ? 0 : -1;
+  }
+  if (need > kNoAllocScratchBytes) {
+    std::fprintf(stderr,
+                 "gemm_launcher_noalloc: M=%d N=%d K=%d needs %zu bytes of repack scratch, more "
+                 "than the fixed %zu-byte buffer; nothing was launched\n",
+                 M, N, K, need, kNoAllocScratchBytes);
+    return -2;
+  }
+  DeviceInfo& d = device_info();
+  void* scratch = noalloc_scratch_ptr();
+  if (scratch == nullptr) return -1;
+  return launch_tc_static_scratch(A, B, C, M, N, K, alpha, beta, stream, d, scratch);
 }
 
 extern "C" GEMM_API int gemm_selftest_wait_timeout(int timeout_us, cudaStream_t stream) {

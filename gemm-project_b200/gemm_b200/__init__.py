@@ -46,6 +46,8 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gemm_slab_rows.restype = i
     lib.gemm_selftest_wait_timeout.argtypes = [i, vp]
     lib.gemm_selftest_wait_timeout.restype = i
+    lib.gemm_launcher_noalloc.argtypes = gemm8 + [vp]
+    lib.gemm_launcher_noalloc.restype = i
     return lib
 
 

@@ -54,6 +54,31 @@ GEMM_API void gemm_launcher_stream(const gemm_half_t* A, const gemm_half_t* B, g
 GEMM_API int gemm_launcher_ex(const gemm_half_t* A, const gemm_half_t* B, gemm_half_t* C, int M, int N,
                      int K, float alpha, float beta, cudaStream_t stream, int path, int tile_n);
 
+/* gemm_launcher_stream for callers that cannot let a library allocate device
+ * memory. No counterpart in the reference.
+ * Who needs it: processes that reserve nearly all free HBM up front (serving
+ * engines that size a cache pool to fill the GPU) and have nothing left for a
+ * library, and frameworks that require every device allocation to go through
+ * their own allocator so that their memory accounting stays exact. For them,
+ * the repack scratch that gemm_launcher_stream takes from cudaMallocAsync (when
+ * A's or B's base is not 16-byte aligned, or K or N is not a multiple of 8, and
+ * the shape goes to the tensor-core kernel) is not an option.
+ * This entry point never calls cudaMalloc, cudaMallocAsync, cudaFree or any
+ * allocating library routine. The repack uses one fixed 32 MiB device buffer
+ * that is part of the library image: every GPU that loads the library holds
+ * it until the process exits. The first call on a device looks up that
+ * buffer's device address, so make the first call on each device before any
+ * stream capture. All calls share the buffer: calls that overlap on the GPU
+ * (other streams, other host threads) race on it and must be serialized by the
+ * caller. Shapes that need no repack run exactly as gemm_launcher_stream.
+ * Returns 0 on success; -2 if the repack would need more than 32 MiB
+ * (M*roundup8(K)*2 rounded up to 256, plus K*roundup8(N)*2 bytes; nothing is
+ * launched and C is untouched; a message goes to stderr); -1 if the buffer's
+ * device address cannot be obtained (see gemm_launcher_status). */
+GEMM_API int gemm_launcher_noalloc(const gemm_half_t* A, const gemm_half_t* B, gemm_half_t* C,
+                                   int M, int N, int K, float alpha, float beta,
+                                   cudaStream_t stream);
+
 /* Sticky status of this library (no counterpart in the reference, which
  * returns nothing and checks no launch, src/gemm.cu:104-134). Returns 0 when
  * every call since the last query launched and no kernel reported an error,
