@@ -199,9 +199,16 @@ def cpu_reference_rate(m, n, k, dist, alpha, beta, budget_s=8.0, threads=None):
 # ---------------------------------------------------------------------------
 # single-GPU workloads
 # ---------------------------------------------------------------------------
-def measure_config(gb, name, cfg, stream, steps, warmup, device):
+def measure_config(gb, name, cfg, stream, steps, warmup, device, tn=False):
     m, n, k = cfg["m"], cfg["n"], cfg["k"]
     a, b, c = dev_inputs(m, n, k, cfg["dist"], cfg.get("c_dist", "uniform"), 0, device)
+    if tn:  # the same product with B given as Bt[N,K] (gemm_launcher_tn)
+        bt = b.t().contiguous()
+        c_t = c.clone()
+        ms_t = time_calls(lambda: gb.gemm_tn(a, bt, c_t, cfg["alpha"], cfg["beta"], stream), steps,
+                          warmup, stream)
+        return {"M": m, "N": n, "K": k, "kernel": gb.last_kernel(), "us": ms_t * 1e3,
+                "tflops": 2.0 * m * n * k / ms_t / 1e9}
     off = cfg.get("offset", 0)
     a, b, c = offset_copy(a, off), offset_copy(b, off), offset_copy(c, off)
     alpha, beta = cfg["alpha"], cfg["beta"]
@@ -477,6 +484,9 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=8.0, help="seconds of CPU baseline work")
     ap.add_argument("--only", default=None,
                     help="time one config of oracle.CONFIGS (ours and cuBLAS) and exit")
+    ap.add_argument("--tn", action="store_true", help="with --only: time gemm_launcher_tn")
+    ap.add_argument("--shape", default=None,
+                    help="with --only: override M,N,K of the config (e.g. 2048,2048,8192)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -502,8 +512,10 @@ def main():
         cfg = dict(CONFIGS[args.only])
         if args.only == "sharded32768":
             cfg["m"] = 4096
+        if args.shape:
+            cfg["m"], cfg["n"], cfg["k"] = (int(x) for x in args.shape.split(","))
         r = measure_config(gb, args.only, cfg, torch.cuda.current_stream(), args.steps,
-                           args.warmup, device)
+                           args.warmup, device, tn=args.tn)
         print(json.dumps({"only": args.only, **r}), flush=True)
         return
     if world > 1:

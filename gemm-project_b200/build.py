@@ -28,7 +28,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 EXPORTS = [
     "gemm_launcher", "gemm_launcher_stream", "gemm_launcher_ex", "gemm_launcher_status",
     "gemm_last_kernel", "gemm_cublas", "gemm_cublas_stream", "gemm_slab_rows",
-    "gemm_selftest_wait_timeout", "gemm_launcher_noalloc",
+    "gemm_selftest_wait_timeout", "gemm_launcher_noalloc", "gemm_launcher_tn",
 ]
 
 

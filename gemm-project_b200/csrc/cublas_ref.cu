@@ -13,7 +13,7 @@
 #include <algorithm>
 #include <cstdio>
 
-#include "../../include/gemm_b200.h"
+#include "gemm_b200.h"
 
 namespace {
 

@@ -26,7 +26,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "../../include/gemm_b200.h"
+#include "gemm_b200.h"
 #include "ptx.cuh"
 #include "skinny.cuh"
 #include "tc_gemm.cuh"
@@ -60,7 +60,10 @@ thread_local const char* tl_last_kernel = "";
 
 struct DeviceInfo {
   int sms = 0;
+  int pair_clusters = 0;          // co-resident 2-CTA clusters, 256 x 256 pair tiles
+  int pair2_clusters = 0;         // co-resident 2-CTA clusters, 512 x 256 pair tiles
   int* err = nullptr;
+  cudaMemPool_t pool = nullptr;   // repack scratch (never trimmed between calls)
   bool configured = false;
 };
 DeviceInfo g_dev[kMaxDevices];
@@ -96,10 +99,43 @@ void log_launch(const char* kernel, int M, int N, int K, dim3 grid, dim3 block) 
   std::fflush(stdout);
 }
 
-template <int BN>
+// Tuning overrides for benchmark sweeps (read once; 0 = built-in choice).
+int env_int(const char* name) {
+  const char* v = std::getenv(name);
+  return v ? std::atoi(v) : 0;
+}
+
+template <int BN, bool PAIR, int SLABS>
 void configure_tc() {
-  cudaFuncSetAttribute(tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       TcCfg<BN>::kSmemBytes);
+  cudaFuncSetAttribute(tc_gemm_kernel<BN, PAIR, false, SLABS>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       TcCfg<BN, PAIR, false, SLABS>::kSmemBytes);
+  cudaFuncSetAttribute(tc_gemm_kernel<BN, PAIR, true, SLABS>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       TcCfg<BN, PAIR, true, SLABS>::kSmemBytes);
+}
+
+// Co-resident 2-CTA clusters of a pair kernel (0 if it cannot be placed).
+template <int SLABS>
+int pair_capacity(int sms) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+  cfg.blockDim = dim3(TcCfg<256, true, false, SLABS>::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = TcCfg<256, true, false, SLABS>::kSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<256, true, false, SLABS>, &cfg) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  return n;
 }
 
 // Per-device one-time set-up: SM count, device error word, kernel attributes.
@@ -114,9 +150,26 @@ DeviceInfo& device_info() {
     void* p = nullptr;
     record_error(cudaGetSymbolAddress(&p, g_device_error));
     d.err = static_cast<int*>(p);
-    configure_tc<64>();
-    configure_tc<128>();
-    configure_tc<256>();
+    configure_tc<64, false, 1>();
+    configure_tc<128, false, 1>();
+    configure_tc<256, false, 1>();
+    configure_tc<256, true, 1>();
+    configure_tc<256, true, 2>();
+    d.pair_clusters = pair_capacity<1>(d.sms);
+    d.pair2_clusters = pair_capacity<2>(d.sms);
+    {
+      cudaMemPoolProps props{};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev;
+      if (cudaMemPoolCreate(&d.pool, &props) == cudaSuccess) {
+        uint64_t keep = ~uint64_t(0);
+        cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep);
+      } else {
+        cudaGetLastError();
+        d.pool = nullptr;
+      }
+    }
     std::atomic_thread_fence(std::memory_order_release);
     d.configured = true;
   }
@@ -173,87 +226,115 @@ void launch_scale(half* C, int M, int N, float beta, cudaStream_t s, const Devic
   record_error(cudaGetLastError());
 }
 
-int choose_tile_n(int M, int N, int sms) {
-  const int tiles_m = ceil_div(M, 128);
-  const int cand[3] = {256, 128, 64};
-  const float eff[3] = {1.0f, 0.9f, 0.65f};
+// Tile shapes of the tcgen05 path (the `tile_n` codes of gemm_launcher_ex):
+// 64, 128, 256 = one CTA per 128 x tile tile; kTilePair = 256 x 256 per 2-CTA
+// cluster; kTilePair2 = 512 x 256 per 2-CTA cluster (two A slabs per CTA).
+constexpr int kTilePair = 2;
+constexpr int kTilePair2 = 3;
+
+bool tile_available(int tile, const DeviceInfo& d) {
+  return tile == 64 || tile == 128 || tile == 256 || (tile == kTilePair && d.pair_clusters > 0) ||
+         (tile == kTilePair2 && d.pair2_clusters > 0);
+}
+
+// Pick the tile that minimises (waves x per-SM tile work / efficiency). The
+// efficiencies rank the shapes by their shared-memory and L2 traffic per FLOP;
+// the wave count models the quantisation of tiles over the SMs.
+int choose_tile(int M, int N, const DeviceInfo& d) {
+  const int forced = env_int("GEMM_TILE");
+  if (forced && tile_available(forced, d)) return forced;
+  struct Cand {
+    int code, tile_m, tile_n, units, sm_cols;
+    float eff;
+  };
+  // sm_cols: output columns x (rows / 128) one SM computes per tile
+  const Cand cands[5] = {{kTilePair2, 512, 256, d.pair2_clusters, 512, 1.1f},
+                         {kTilePair, 256, 256, d.pair_clusters, 256, 1.0f},
+                         {256, 128, 256, d.sms, 256, 0.95f},
+                         {128, 128, 128, d.sms, 128, 0.8f},
+                         {64, 128, 64, d.sms, 64, 0.6f}};
   int best = 256;
   float best_cost = 1e30f;
-  for (int i = 0; i < 3; ++i) {
-    const int tiles = tiles_m * ceil_div(N, cand[i]);
-    const int waves = ceil_div(tiles, sms);
-    const float cost = waves * cand[i] / eff[i];
+  for (const Cand& c : cands) {
+    if (c.units <= 0) continue;
+    const long tiles = static_cast<long>(ceil_div(M, c.tile_m)) * ceil_div(N, c.tile_n);
+    const long waves = (tiles + c.units - 1) / c.units;
+    const float cost = static_cast<float>(waves) * c.sm_cols / c.eff;
     if (cost < best_cost) {
       best_cost = cost;
-      best = cand[i];
+      best = c.code;
     }
   }
   return best;
 }
 
-template <int BN>
-void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, int sms,
-                  cudaStream_t s, int M, int N, int K) {
-  const int tiles = p.tiles_m * p.tiles_n;
-  const int grid = std::min(tiles, sms);
-  static const char* names[3] = {"tc_gemm_kernel<128x64>", "tc_gemm_kernel<128x128>",
-                                 "tc_gemm_kernel<128x256>"};
-  log_launch(names[BN == 64 ? 0 : (BN == 128 ? 1 : 2)], M, N, K, dim3(grid),
-             dim3(TcCfg<BN>::kThreads));
-  tc_gemm_kernel<BN><<<grid, TcCfg<BN>::kThreads, TcCfg<BN>::kSmemBytes, s>>>(ta, tb, p);
-  record_error(cudaGetLastError());
+int raster_group(int tiles_m) {
+  const int g = env_int("GEMM_RASTER_GROUP");
+  return std::max(1, std::min(tiles_m, g > 0 ? g : 8));
 }
 
-int launch_tc(const half* A, const half* B, half* C, int M, int N, int K, float alpha, float beta,
-              cudaStream_t s, int tile_n, const DeviceInfo& d) {
-  const bool a_ok = aligned16(A) && K % 8 == 0;
-  const bool b_ok = aligned16(B) && N % 8 == 0;
-  const half* a_src = A;
-  const half* b_src = B;
-  int lda = K, ldb = N;
-  void* scratch = nullptr;
-  size_t a_bytes = 0, b_bytes = 0;
-  if (!a_ok) a_bytes = static_cast<size_t>(M) * round_up8(K) * sizeof(half);
-  if (!b_ok) b_bytes = static_cast<size_t>(K) * round_up8(N) * sizeof(half);
-  a_bytes = (a_bytes + 255) / 256 * 256;
-  if (a_bytes + b_bytes) {
-    cudaError_t e = cudaMallocAsync(&scratch, a_bytes + b_bytes, s);
-    if (e != cudaSuccess) {
-      record_error(e);
-      return -1;
-    }
-    const int threads = 256;
-    if (!a_ok) {
-      lda = round_up8(K);
-      half* dst = static_cast<half*>(scratch);
-      const size_t work = static_cast<size_t>(M) * ceil_div(K, 8);
-      const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
-      log_launch("pack_rows_kernel<A>", M, N, K, dim3(blocks), dim3(threads));
-      pack_rows_kernel<<<blocks, threads, 0, s>>>(A, K, dst, lda, M, K);
-      record_error(cudaGetLastError());
-      a_src = dst;
-    }
-    if (!b_ok) {
-      ldb = round_up8(N);
-      half* dst = reinterpret_cast<half*>(static_cast<char*>(scratch) + a_bytes);
-      const size_t work = static_cast<size_t>(K) * ceil_div(N, 8);
-      const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
-      log_launch("pack_rows_kernel<B>", M, N, K, dim3(blocks), dim3(threads));
-      pack_rows_kernel<<<blocks, threads, 0, s>>>(B, N, dst, ldb, K, N);
-      record_error(cudaGetLastError());
-      b_src = dst;
-    }
+template <int BN, bool PAIR, bool BKM, int SLABS>
+void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                  const TcParams& p, const DeviceInfo& d, cudaStream_t s, int M, int N, int K) {
+  using Cfg = TcCfg<BN, PAIR, BKM, SLABS>;
+  const int tiles = p.tiles_m * p.tiles_n;
+  static const char* names[2][5] = {
+      {"tc_gemm_kernel<128x64>", "tc_gemm_kernel<128x128>", "tc_gemm_kernel<128x256>",
+       "tc_gemm_kernel<256x256,pair>", "tc_gemm_kernel<512x256,pair>"},
+      {"tc_gemm_kernel<128x64,tn>", "tc_gemm_kernel<128x128,tn>", "tc_gemm_kernel<128x256,tn>",
+       "tc_gemm_kernel<256x256,pair,tn>", "tc_gemm_kernel<512x256,pair,tn>"}};
+  const int idx = PAIR ? (SLABS == 2 ? 4 : 3) : (BN == 64 ? 0 : (BN == 128 ? 1 : 2));
+  const char* name = names[BKM ? 1 : 0][idx];
+  if constexpr (PAIR) {
+    const int cap = SLABS == 2 ? d.pair2_clusters : d.pair_clusters;
+    const int clusters = std::min(tiles, cap);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    log_launch(name, M, N, K, cfg.gridDim, cfg.blockDim);
+    record_error(cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, true, BKM, SLABS>, ta, tb, tc, p));
+  } else {
+    const int grid = std::min(tiles, d.sms);
+    log_launch(name, M, N, K, dim3(grid), dim3(Cfg::kThreads));
+    tc_gemm_kernel<BN, false, BKM, SLABS><<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(ta, tb, tc, p);
+    record_error(cudaGetLastError());
   }
+}
 
-  int bn = tile_n ? tile_n : choose_tile_n(M, N, d.sms);
-  CUtensorMap ta, tb;
-  bool ok = make_tmap(&ta, a_src, K, M, static_cast<uint64_t>(lda) * 2, 64, 128) &&
-            make_tmap(&tb, b_src, N, K, static_cast<uint64_t>(ldb) * 2, 64, 64);
-  if (!ok) {
+// Encode the tensor maps and launch the tcgen05 kernel for `tile` on operands
+// that are TMA-addressable as given (pitches lda/ldb in elements).
+// b_kmajor: B is given as Bt[N,K] (row pitch ldb), i.e. C = A * Bt^T.
+int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half* C, int M, int N,
+                   int K, float alpha, float beta, cudaStream_t s, int tile, const DeviceInfo& d,
+                   bool b_kmajor = false) {
+  const bool pair = tile == kTilePair || tile == kTilePair2;
+  const int slabs = tile == kTilePair2 ? 2 : 1;
+  CUtensorMap ta, tb, tc;
+  std::memset(&tc, 0, sizeof(tc));
+  const uint32_t b_rows = pair ? 128u : static_cast<uint32_t>(tile);
+  const bool ok_b = b_kmajor
+                        ? make_tmap(&tb, b_src, K, N, static_cast<uint64_t>(ldb) * 2, 64, b_rows)
+                        : make_tmap(&tb, b_src, N, K, static_cast<uint64_t>(ldb) * 2, 64, 64);
+  const bool ok_a =
+      make_tmap(&ta, a_src, K, M, static_cast<uint64_t>(lda) * 2, 64, 128u * slabs);
+  // C goes through TMA (32 rows x 64 columns boxes) when it is TMA-addressable.
+  const int c_tma = aligned16(C) && N % 8 == 0 &&
+                    make_tmap(&tc, C, N, M, static_cast<uint64_t>(N) * 2, 64, 32);
+  if (!(ok_a && ok_b)) {
     record_error(cudaErrorInvalidValue);
-    if (scratch) cudaFreeAsync(scratch, s);
     return -1;
   }
+  const int tile_m = pair ? 256 * slabs : 128;
+  const int tile_n = pair ? 256 : tile;
   TcParams p{};
   p.C = C;
   p.M = M;
@@ -262,20 +343,105 @@ int launch_tc(const half* A, const half* B, half* C, int M, int N, int K, float 
   p.ldc = N;
   p.alpha = alpha;
   p.beta = beta;
-  p.tiles_m = ceil_div(M, 128);
-  p.tiles_n = ceil_div(N, bn);
+  p.tiles_m = ceil_div(M, tile_m);
+  p.tiles_n = ceil_div(N, tile_n);
   p.num_kb = ceil_div(K, 64);
-  p.group = std::min(p.tiles_m, 8);
+  p.group = raster_group(p.tiles_m);
+  p.c_tma = c_tma;
   p.c_vec_ok = aligned16(C) && N % 8 == 0;
   p.timeout_ns = wait_timeout_ns();
   p.err = d.err;
-  switch (bn) {
-    case 64: launch_tc_bn<64>(ta, tb, p, d.sms, s, M, N, K); break;
-    case 128: launch_tc_bn<128>(ta, tb, p, d.sms, s, M, N, K); break;
-    default: launch_tc_bn<256>(ta, tb, p, d.sms, s, M, N, K); break;
+  if (b_kmajor) {
+    switch (tile) {
+      case 64: launch_tc_bn<64, false, true, 1>(ta, tb, tc, p, d, s, M, N, K); break;
+      case 128: launch_tc_bn<128, false, true, 1>(ta, tb, tc, p, d, s, M, N, K); break;
+      case kTilePair: launch_tc_bn<256, true, true, 1>(ta, tb, tc, p, d, s, M, N, K); break;
+      case kTilePair2: launch_tc_bn<256, true, true, 2>(ta, tb, tc, p, d, s, M, N, K); break;
+      default: launch_tc_bn<256, false, true, 1>(ta, tb, tc, p, d, s, M, N, K); break;
+    }
+  } else {
+    switch (tile) {
+      case 64: launch_tc_bn<64, false, false, 1>(ta, tb, tc, p, d, s, M, N, K); break;
+      case 128: launch_tc_bn<128, false, false, 1>(ta, tb, tc, p, d, s, M, N, K); break;
+      case kTilePair: launch_tc_bn<256, true, false, 1>(ta, tb, tc, p, d, s, M, N, K); break;
+      case kTilePair2: launch_tc_bn<256, true, false, 2>(ta, tb, tc, p, d, s, M, N, K); break;
+      default: launch_tc_bn<256, false, false, 1>(ta, tb, tc, p, d, s, M, N, K); break;
+    }
   }
-  if (scratch) cudaFreeAsync(scratch, s);
   return 0;
+}
+
+// Bytes of repack scratch the tcgen05 path needs for these operands (0 when
+// both are TMA-addressable as they are). A's share is rounded up to 256 bytes
+// so that B's copy starts aligned.
+size_t repack_bytes(const half* A, const half* B, int M, int N, int K) {
+  size_t a_bytes = 0, b_bytes = 0;
+  if (!(aligned16(A) && K % 8 == 0)) a_bytes = static_cast<size_t>(M) * round_up8(K) * sizeof(half);
+  if (!(aligned16(B) && N % 8 == 0)) b_bytes = static_cast<size_t>(K) * round_up8(N) * sizeof(half);
+  return (a_bytes + 255) / 256 * 256 + b_bytes;
+}
+
+// Copy whichever of A and B is not TMA-addressable into `scratch` (laid out as
+// repack_bytes() describes) with its pitch rounded up to 8 halves, and point
+// a_src/b_src (pitches lda/ldb) at the operands the kernel should read.
+void repack_operands(const half* A, const half* B, int M, int N, int K, cudaStream_t s,
+                     const DeviceInfo& d, void* scratch, const char* const names[2],
+                     const half** a_src, int* lda, const half** b_src, int* ldb) {
+  const bool a_ok = aligned16(A) && K % 8 == 0;
+  const bool b_ok = aligned16(B) && N % 8 == 0;
+  *a_src = A;
+  *lda = K;
+  *b_src = B;
+  *ldb = N;
+  size_t a_bytes = a_ok ? 0 : static_cast<size_t>(M) * round_up8(K) * sizeof(half);
+  a_bytes = (a_bytes + 255) / 256 * 256;
+  const int threads = 256;
+  if (!a_ok) {
+    half* dst = static_cast<half*>(scratch);
+    const size_t work = static_cast<size_t>(M) * ceil_div(K, 8);
+    const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
+    log_launch(names[0], M, N, K, dim3(blocks), dim3(threads));
+    pack_rows_kernel<<<blocks, threads, 0, s>>>(A, K, dst, round_up8(K), M, K);
+    record_error(cudaGetLastError());
+    *a_src = dst;
+    *lda = round_up8(K);
+  }
+  if (!b_ok) {
+    half* dst = reinterpret_cast<half*>(static_cast<char*>(scratch) + a_bytes);
+    const size_t work = static_cast<size_t>(K) * ceil_div(N, 8);
+    const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
+    log_launch(names[1], M, N, K, dim3(blocks), dim3(threads));
+    pack_rows_kernel<<<blocks, threads, 0, s>>>(B, N, dst, round_up8(N), K, N);
+    record_error(cudaGetLastError());
+    *b_src = dst;
+    *ldb = round_up8(N);
+  }
+}
+
+int launch_tc(const half* A, const half* B, half* C, int M, int N, int K, float alpha, float beta,
+              cudaStream_t s, int tile, const DeviceInfo& d) {
+  if (tile != 0 && !tile_available(tile, d)) tile = 256;
+  if (tile == 0) tile = choose_tile(M, N, d);
+  const size_t need = repack_bytes(A, B, M, N, K);
+  const half* a_src = A;
+  const half* b_src = B;
+  int lda = K, ldb = N;
+  void* scratch = nullptr;
+  if (need) {
+    // Stream-ordered scratch from this library's pool (never trimmed between
+    // calls, so steady-state calls reuse the same memory without a sync).
+    const cudaError_t e = d.pool ? cudaMallocFromPoolAsync(&scratch, need, d.pool, s)
+                                 : cudaMallocAsync(&scratch, need, s);
+    if (e != cudaSuccess) {
+      record_error(e);
+      return -1;
+    }
+    static const char* const names[2] = {"pack_rows_kernel<A>", "pack_rows_kernel<B>"};
+    repack_operands(A, B, M, N, K, s, d, scratch, names, &a_src, &lda, &b_src, &ldb);
+  }
+  const int rc = launch_tc_core(a_src, lda, b_src, ldb, C, M, N, K, alpha, beta, s, tile, d);
+  if (scratch) cudaFreeAsync(scratch, s);
+  return rc;
 }
 
 template <int MR, bool VEC>
@@ -374,7 +540,9 @@ int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float a
     launch_scale(C, M, N, beta, s, d);
     return 0;
   }
-  if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256) return -1;
+  if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256 && tile_n != kTilePair &&
+      tile_n != kTilePair2)
+    return -1;
   if (path == 0) {
     if (M <= 8)
       path = 2;
@@ -389,6 +557,61 @@ int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float a
     case 3: return launch_col(A, B, C, M, N, K, alpha, beta, s, d);
     default: return -1;
   }
+}
+
+// C = A * Bt^T with Bt given as [N,K] row-major (the layout of a linear layer's
+// weight). Same kernels with B read K-major, so no transpose pass is needed.
+int launch_tn(const half* A, const half* Bt, half* C, int M, int N, int K, float alpha,
+              float beta, cudaStream_t s, int tile) {
+  if (M <= 0 || N <= 0) return 0;
+  DeviceInfo& d = device_info();
+  if (K <= 0) {
+    launch_scale(C, M, N, beta, s, d);
+    return 0;
+  }
+  if (tile != 0 && !tile_available(tile, d)) tile = 256;
+  if (tile == 0) tile = choose_tile(M, N, d);
+  const bool a_ok = aligned16(A) && K % 8 == 0;
+  const bool b_ok = aligned16(Bt) && K % 8 == 0;
+  size_t a_bytes = a_ok ? 0 : static_cast<size_t>(M) * round_up8(K) * sizeof(half);
+  a_bytes = (a_bytes + 255) / 256 * 256;
+  const size_t b_bytes = b_ok ? 0 : static_cast<size_t>(N) * round_up8(K) * sizeof(half);
+  const half* a_src = A;
+  const half* b_src = Bt;
+  int lda = K, ldb = K;
+  void* scratch = nullptr;
+  if (a_bytes + b_bytes) {
+    const cudaError_t e = d.pool ? cudaMallocFromPoolAsync(&scratch, a_bytes + b_bytes, d.pool, s)
+                                 : cudaMallocAsync(&scratch, a_bytes + b_bytes, s);
+    if (e != cudaSuccess) {
+      record_error(e);
+      return -1;
+    }
+    const int threads = 256;
+    if (!a_ok) {
+      half* dst = static_cast<half*>(scratch);
+      const size_t work = static_cast<size_t>(M) * ceil_div(K, 8);
+      const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
+      log_launch("pack_rows_kernel<A>", M, N, K, dim3(blocks), dim3(threads));
+      pack_rows_kernel<<<blocks, threads, 0, s>>>(A, K, dst, round_up8(K), M, K);
+      record_error(cudaGetLastError());
+      a_src = dst;
+      lda = round_up8(K);
+    }
+    if (!b_ok) {
+      half* dst = reinterpret_cast<half*>(static_cast<char*>(scratch) + a_bytes);
+      const size_t work = static_cast<size_t>(N) * ceil_div(K, 8);
+      const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
+      log_launch("pack_rows_kernel<Bt>", M, N, K, dim3(blocks), dim3(threads));
+      pack_rows_kernel<<<blocks, threads, 0, s>>>(Bt, K, dst, round_up8(K), N, K);
+      record_error(cudaGetLastError());
+      b_src = dst;
+      ldb = round_up8(K);
+    }
+  }
+  const int rc = launch_tc_core(a_src, lda, b_src, ldb, C, M, N, K, alpha, beta, s, tile, d, true);
+  if (scratch) cudaFreeAsync(scratch, s);
+  return rc;
 }
 
 // ---------------------------------------------------------------------------
@@ -441,76 +664,16 @@ void* noalloc_scratch_ptr() {
   return s.ptr;
 }
 
-// Bytes of repack scratch the tcgen05 path needs for these operands (0 when
-// both are TMA-addressable as they are). A's share is rounded up to 256 bytes
-// so that B's copy starts aligned.
-size_t repack_bytes(const half* A, const half* B, int M, int N, int K) {
-  size_t a_bytes = 0, b_bytes = 0;
-  if (!(aligned16(A) && K % 8 == 0)) a_bytes = static_cast<size_t>(M) * round_up8(K) * sizeof(half);
-  if (!(aligned16(B) && N % 8 == 0)) b_bytes = static_cast<size_t>(K) * round_up8(N) * sizeof(half);
-  return (a_bytes + 255) / 256 * 256 + b_bytes;
-}
-
-// The repack + tcgen05 path with caller-provided scratch (no allocation).
+// The repack + tcgen05 path with the fixed scratch buffer (no allocation).
 int launch_tc_static_scratch(const half* A, const half* B, half* C, int M, int N, int K,
                              float alpha, float beta, cudaStream_t s, const DeviceInfo& d,
                              void* scratch) {
-  const bool a_ok = aligned16(A) && K % 8 == 0;
-  const bool b_ok = aligned16(B) && N % 8 == 0;
-  const half* a_src = A;
-  const half* b_src = B;
-  int lda = K, ldb = N;
-  size_t a_bytes = a_ok ? 0 : static_cast<size_t>(M) * round_up8(K) * sizeof(half);
-  a_bytes = (a_bytes + 255) / 256 * 256;
-  const int threads = 256;
-  if (!a_ok) {
-    lda = round_up8(K);
-    half* dst = static_cast<half*>(scratch);
-    const size_t work = static_cast<size_t>(M) * ceil_div(K, 8);
-    const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
-    log_launch("pack_rows_kernel<A,static>", M, N, K, dim3(blocks), dim3(threads));
-    pack_rows_kernel<<<blocks, threads, 0, s>>>(A, K, dst, lda, M, K);
-    record_error(cudaGetLastError());
-    a_src = dst;
-  }
-  if (!b_ok) {
-    ldb = round_up8(N);
-    half* dst = reinterpret_cast<half*>(static_cast<char*>(scratch) + a_bytes);
-    const size_t work = static_cast<size_t>(K) * ceil_div(N, 8);
-    const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
-    log_launch("pack_rows_kernel<B,static>", M, N, K, dim3(blocks), dim3(threads));
-    pack_rows_kernel<<<blocks, threads, 0, s>>>(B, N, dst, ldb, K, N);
-    record_error(cudaGetLastError());
-    b_src = dst;
-  }
-  const int bn = choose_tile_n(M, N, d.sms);
-  CUtensorMap ta, tb;
-  if (!(make_tmap(&ta, a_src, K, M, static_cast<uint64_t>(lda) * 2, 64, 128) &&
-        make_tmap(&tb, b_src, N, K, static_cast<uint64_t>(ldb) * 2, 64, 64))) {
-    record_error(cudaErrorInvalidValue);
-    return -1;
-  }
-  TcParams p{};
-  p.C = C;
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  p.ldc = N;
-  p.alpha = alpha;
-  p.beta = beta;
-  p.tiles_m = ceil_div(M, 128);
-  p.tiles_n = ceil_div(N, bn);
-  p.num_kb = ceil_div(K, 64);
-  p.group = std::min(p.tiles_m, 8);
-  p.c_vec_ok = aligned16(C) && N % 8 == 0;
-  p.timeout_ns = wait_timeout_ns();
-  p.err = d.err;
-  switch (bn) {
-    case 64: launch_tc_bn<64>(ta, tb, p, d.sms, s, M, N, K); break;
-    case 128: launch_tc_bn<128>(ta, tb, p, d.sms, s, M, N, K); break;
-    default: launch_tc_bn<256>(ta, tb, p, d.sms, s, M, N, K); break;
-  }
-  return 0;
+  static const char* const names[2] = {"pack_rows_kernel<A,static>", "pack_rows_kernel<B,static>"};
+  const half* a_src;
+  const half* b_src;
+  int lda, ldb;
+  repack_operands(A, B, M, N, K, s, d, scratch, names, &a_src, &lda, &b_src, &ldb);
+  return launch_tc_core(a_src, lda, b_src, ldb, C, M, N, K, alpha, beta, s, choose_tile(M, N, d), d);
 }
 
 }  // namespace
@@ -553,6 +716,15 @@ extern "C" GEMM_API int gemm_slab_rows(int M, int world, int rank, int* row0) {
   const int base = M / world, extra = M % world;
   *row0 = rank * base + std::min(rank, extra);
   return base + (rank < extra ? 1 : 0);
+}
+
+extern "C" GEMM_API int gemm_launcher_tn(const half* A, const half* Bt, half* C, int M, int N,
+                                         int K, float alpha, float beta, cudaStream_t stream,
+                                         int tile_n) {
+  if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256 && tile_n != kTilePair &&
+      tile_n != kTilePair2)
+    return -1;
+  return launch_tn(A, Bt, C, M, N, K, alpha, beta, stream, tile_n);
 }
 
 extern "C" GEMM_API int gemm_launcher_noalloc(const half* A, const half* B, half* C, int M, int N,

@@ -1,8 +1,9 @@
 // Persistent, warp-specialized tcgen05 GEMM for sm_100a.
 //
 //   C[M,N] = half_rn(alpha * FP32acc(A[M,K] * B[K,N]) + beta * float(C))
-//   A row-major (K-major operand), B row-major (N-major = "MN-major" operand),
-//   C row-major, C read only when beta != 0.
+//   A row-major (K-major operand); B row-major [K,N] (N-major, "MN-major"
+//   operand) or, for the TN entry point, Bt[N,K] (K-major); C row-major, read
+//   only when beta != 0.
 //
 // Replaces the reference's tensor-core kernels on the launcher path
 // (src/lib/gemm_llm_kernels.cuh:272-662 gemm_mma_llm_kernel, and
@@ -10,20 +11,38 @@
 // are mma.sync kernels fed by cp.async. Same arithmetic contract: FP16 inputs,
 // FP32 accumulation, epilogue fmaf(alpha, acc, beta * C) rounded to nearest.
 //
-// Structure (one CTA per SM, grid-stride over output tiles of BM x BN):
-//   warp 0        TMA producer: one lane streams A (BM x 64) and B (64 x BN)
-//                 tiles into a kStages-deep ring of 128B-swizzled smem buffers,
-//                 signalling `full[s]` through mbarrier transaction counts.
-//   warp 1        TMEM owner and UMMA issuer: one lane issues
-//                 tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) into a
-//                 double-buffered FP32 accumulator in TMEM, frees smem stages
-//                 with tcgen05.commit -> `empty[s]`, and publishes finished
-//                 accumulators with tcgen05.commit -> `tmem_full[a]`.
-//   warps 2..5    epilogue: tcgen05.ld 32 lanes x 32 columns per warp, apply
-//                 alpha/beta in FP32, round to half, store; then release the
-//                 accumulator through `tmem_empty[a]`, so the epilogue of tile i
-//                 overlaps the main loop of tile i+1.
-// Every mbarrier wait is bounded (see ptx.cuh mbar_wait): on expiry the kernel
+// Tile shapes (template parameters):
+//   single CTA, 1 slab:  128 x BN per CTA (BN = 64, 128, 256), cta_group::1.
+//   CTA pair,  1 slab:  256 x 256 per 2-CTA cluster, cta_group::2: each CTA
+//                        holds 128 rows of A and 128 of the 256 B columns.
+//   CTA pair,  2 slabs: 512 x 256 per 2-CTA cluster: each CTA holds two
+//                        128-row A slabs and 128 B columns; per K step two
+//                        UMMAs (one per slab) share the B half, so shared-memory
+//                        and L2 traffic per FLOP drop by a quarter.
+// The FP32 accumulator lives in TMEM (lane = output row, column = output
+// column); with one slab it is double-buffered across tiles, with two slabs
+// the two slabs fill TMEM and are released one at a time, so the drain of a
+// slab overlaps the next tile's first UMMAs of the other slab.
+//
+// Roles (192 threads per CTA, grid-stride over tiles, grouped raster):
+//   warp 0        TMA producer: one lane streams A (rows x 64) and B boxes into
+//                 a kStages-deep ring of 128B-swizzled smem stages. A stage's
+//                 `full` mbarrier (in the pair's even CTA) counts the bytes of
+//                 both CTAs.
+//   warp 1        TMEM owner; one lane of the even CTA issues the UMMAs (K = 16
+//                 each, four per 64-wide stage and slab), frees stages with
+//                 tcgen05.commit -> `empty[s]` of both CTAs and publishes each
+//                 finished slab with tcgen05.commit -> `tmem_full` of both CTAs.
+//   warps 2..5    epilogue, one TMEM lane quadrant each: tcgen05.ld 32 rows x
+//                 64 columns, alpha/beta in FP32, round to half. When C is
+//                 TMA-addressable: C box TMA-loaded into a 128B-swizzled staging
+//                 tile (beta != 0), result written back there, TMA-stored (out-
+//                 of-range rows/columns are clipped by the hardware). Otherwise:
+//                 transpose through a padded smem tile, per-element predicated
+//                 stores. The slab's accumulator is released right after its
+//                 last tcgen05.ld.
+// No TMA load uses cluster multicast, and no operand is another GPU's memory.
+// Every mbarrier wait is bounded (ptx.cuh mbar_wait): on expiry the kernel
 // records an error code and unwinds; it never traps.
 #pragma once
 
@@ -31,23 +50,46 @@
 
 namespace gemm_b200 {
 
-template <int BN_>
+template <int BN_, bool PAIR_, bool BKM_ = false, int SLABS_ = 1>
 struct TcCfg {
-  static constexpr int BM = 128;
-  static constexpr int BN = BN_;
-  static constexpr int BK = 64;  // one 128-byte swizzle row of FP16
-  static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
-  static constexpr int kABytes = BM * BK * 2;         // 16 KiB
-  static constexpr int kBBoxBytes = 64 * BK * 2;       // one 64(N) x 64(K) TMA box, 8 KiB
-  static constexpr int kBBytes = BN * BK * 2;          // BN/64 boxes
+  static constexpr bool kPair = PAIR_;
+  static constexpr bool kBKMajor = BKM_;                // B given as Bt[N,K]
+  static constexpr int kSlabs = SLABS_;                 // 128-row A slabs per CTA
+  static constexpr int BM = 128;                        // rows per slab
+  static constexpr int BN = BN_;                        // output columns per tile
+  static constexpr int kMmaM = kPair ? 256 : 128;       // M of one UMMA
+  static constexpr int kCtaRows = BM * kSlabs;          // output rows per CTA
+  static constexpr int kTileM = kCtaRows * (kPair ? 2 : 1);
+  static constexpr int kBCols = kPair ? BN / 2 : BN;    // B columns held by one CTA
+  static constexpr int BK = 64;                         // one 128-byte swizzle row of FP16
+  static constexpr int kSlabBytes = BM * BK * 2;        // 16 KiB
+  static constexpr int kABytes = kCtaRows * BK * 2;
+  // B boxes: N-major B as 64(N) x 64(K) boxes of 8 KiB; K-major B as one box
+  // of kBCols rows x 64 K.
+  static constexpr int kBBoxBytes = BKM_ ? kBCols * BK * 2 : 64 * BK * 2;
+  static constexpr int kBBytes = kBCols * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;  // two accumulators
+  static constexpr int kEpiWarps = 4;
+  static constexpr int kEpiChunk = 64;                  // columns per epilogue chunk
+  static constexpr int kEpiBufBytes = 32 * kEpiChunk * 2;           // 32 rows x 128 B
+  static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;   // double-buffered
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;  // +1024 for alignment
+  static constexpr int kSmemLimit = 227 * 1024;
+  static constexpr int kStagesFit = (kSmemLimit - kEpiBytes - kBarBytes - 1024) / kStageBytes;
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+  static constexpr int kAccCols = kSlabs * BN;          // TMEM columns of one accumulator
+  static constexpr int kAccBufs = 512 / kAccCols >= 2 ? 2 : 1;
+  static constexpr int kTmemCols = kAccBufs * kAccCols < 32 ? 32 : kAccBufs * kAccCols;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + kBarBytes + 1024;
   static constexpr int kThreads = 192;
-  static constexpr int kEpiThreads = 128;
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
-  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+  static_assert(!kPair || BN == 256, "the CTA pair runs 256-column tiles");
+  static_assert(kSlabs == 1 || (kSlabs == 2 && kPair), "two slabs only for the CTA pair");
+  static_assert(kStages >= 3, "pipeline depth");
+  static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
+  static_assert(kTmemCols <= 512, "TMEM columns");
+  // transposed-store fallback uses 32 x 33 floats per warp inside the staging area
+  static_assert(kEpiWarps * 32 * 33 * 4 <= kEpiBytes, "fallback staging fits");
 };
 
 struct TcParams {
@@ -57,7 +99,8 @@ struct TcParams {
   float alpha, beta;
   int tiles_m, tiles_n, num_kb;
   int group;             // grouped raster: tile rows per group
-  int c_vec_ok;          // C base 16B-aligned and ldc % 8 == 0
+  int c_tma;             // C is TMA-addressable: TMA load/store epilogue
+  int c_vec_ok;          // C base 16B-aligned and ldc % 8 == 0 (LSU fallback)
   unsigned long long timeout_ns;
   int* err;
 };
@@ -79,49 +122,74 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16)));
 }
 
-// Store 32 consecutive accumulator columns of one output row.
-__device__ __forceinline__ void epilogue_store32(const TcParams& p, int row, int col0,
-                                                 const uint32_t (&r)[32]) {
-  if (row >= p.M) return;
-  half* crow = p.C + static_cast<size_t>(row) * p.ldc;
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  return static_cast<uint32_t>(__half_as_ushort(__float2half_rn(lo))) |
+         (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(hi))) << 16);
+}
+
+// ---------------------------------------------------------------------------
+// LSU epilogue (C not TMA-addressable): 32 rows x 32 columns per call, lane =
+// row in `r`, transposed through a padded smem tile so that each store
+// instruction covers contiguous row segments.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool chunk_is_vector(const TcParams& p, int col0) {
+  return p.c_vec_ok && col0 + 32 <= p.N;
+}
+
+__device__ __forceinline__ void epilogue_chunk_lsu(const TcParams& p, float* tile, int row_base,
+                                                   int col0, const uint32_t* r, int lane) {
+  constexpr int LD = 33;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) tile[lane * LD + j] = __uint_as_float(r[j]);
+  __syncwarp();
   const bool read_c = p.beta != 0.0f;
-  if (p.c_vec_ok && col0 + 32 <= p.N) {
+  if (chunk_is_vector(p, col0)) {
+    // lane -> row (lane / 4) of an 8-row band, 8-column group (lane % 4)
+    const int cg = (lane & 3) * 8;
 #pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      uint4 prev = make_uint4(0, 0, 0, 0);
-      if (read_c) prev = *reinterpret_cast<const uint4*>(crow + col0 + 8 * v);
-      const uint32_t pw[4] = {prev.x, prev.y, prev.z, prev.w};
-      uint32_t out[4];
+    for (int band = 0; band < 4; ++band) {
+      const int rr = band * 8 + (lane >> 2);
+      const int row = row_base + rr;
+      if (row < p.M) {
+        half* dst = p.C + static_cast<size_t>(row) * p.ldc + col0 + cg;
+        uint4 prev = make_uint4(0, 0, 0, 0);
+        if (read_c) prev = *reinterpret_cast<const uint4*>(dst);
+        const uint32_t pw[4] = {prev.x, prev.y, prev.z, prev.w};
+        uint32_t out[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float c0 = read_c ? half_bits_to_float(pw[j] & 0xFFFFu) : 0.0f;
-        const float c1 = read_c ? half_bits_to_float(pw[j] >> 16) : 0.0f;
-        const float a0 = __uint_as_float(r[8 * v + 2 * j]);
-        const float a1 = __uint_as_float(r[8 * v + 2 * j + 1]);
-        const half h0 = __float2half_rn(fmaf(p.alpha, a0, p.beta * c0));
-        const half h1 = __float2half_rn(fmaf(p.alpha, a1, p.beta * c1));
-        out[j] = static_cast<uint32_t>(__half_as_ushort(h0)) |
-                 (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
+        for (int j = 0; j < 4; ++j) {
+          const float c0 = read_c ? half_bits_to_float(pw[j] & 0xFFFFu) : 0.0f;
+          const float c1 = read_c ? half_bits_to_float(pw[j] >> 16) : 0.0f;
+          out[j] = pack_half2(fmaf(p.alpha, tile[rr * LD + cg + 2 * j], p.beta * c0),
+                              fmaf(p.alpha, tile[rr * LD + cg + 2 * j + 1], p.beta * c1));
+        }
+        *reinterpret_cast<uint4*>(dst) = make_uint4(out[0], out[1], out[2], out[3]);
       }
-      *reinterpret_cast<uint4*>(crow + col0 + 8 * v) = make_uint4(out[0], out[1], out[2], out[3]);
     }
   } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int col = col0 + j;
-      if (col < p.N) {
-        const float prev = read_c ? __half2float(crow[col]) : 0.0f;
-        crow[col] = __float2half_rn(fmaf(p.alpha, __uint_as_float(r[j]), p.beta * prev));
+    // lane -> column; each store instruction one contiguous 64-byte run
+    const int col = col0 + lane;
+    if (col < p.N) {
+#pragma unroll 4
+      for (int rr = 0; rr < 32; ++rr) {
+        const int row = row_base + rr;
+        if (row < p.M) {
+          half* dst = p.C + static_cast<size_t>(row) * p.ldc + col;
+          const float prev = read_c ? __half2float(*dst) : 0.0f;
+          *dst = __float2half_rn(fmaf(p.alpha, tile[rr * LD + lane], p.beta * prev));
+        }
       }
     }
   }
+  __syncwarp();
 }
 
-template <int BN>
-__global__ void __launch_bounds__(TcCfg<BN>::kThreads, 1)
+template <int BN, bool PAIR, bool BKM, int SLABS>
+__global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                   const __grid_constant__ CUtensorMap tmap_b, const TcParams p) {
-  using Cfg = TcCfg<BN>;
+                   const __grid_constant__ CUtensorMap tmap_b,
+                   const __grid_constant__ CUtensorMap tmap_c, const TcParams p) {
+  using Cfg = TcCfg<BN, PAIR, BKM, SLABS>;
   constexpr int kStages = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
 
@@ -131,70 +199,109 @@ __global__ void __launch_bounds__(TcCfg<BN>::kThreads, 1)
   const uint32_t sbase = raw_base + pad;
   const uint32_t sA0 = sbase;
   const uint32_t sB0 = sbase + kStages * Cfg::kABytes;
-  uint8_t* bar_area = smem + kStages * Cfg::kStageBytes;
-  const uint32_t bar0 = sbase + kStages * Cfg::kStageBytes;
-  // Barrier slots (8 bytes each): full[kStages], empty[kStages], tmem_full[2],
-  // tmem_empty[2], final; then the TMEM base address and the abort flag.
+  const uint32_t sEpi = sbase + kStages * Cfg::kStageBytes;  // 1024-aligned
+  float* epi_float = reinterpret_cast<float*>(smem + kStages * Cfg::kStageBytes);
+  uint8_t* bar_area = smem + kStages * Cfg::kStageBytes + Cfg::kEpiBytes;
+  const uint32_t bar0 = sEpi + Cfg::kEpiBytes;
+  // Barrier slots (8 bytes each): full[kStages], empty[kStages],
+  // tmem_full[2][SLABS], tmem_empty[2][SLABS], final, cload[kEpiWarps][2] (one
+  // per C staging buffer); then the TMEM base address and the abort flag.
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (kStages + s); };
-  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kStages + a); };
-  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kStages + 2 + a); };
-  const uint32_t final_bar = bar0 + 8u * (2 * kStages + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_area + 8 * (2 * kStages + 5));
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_area + 8 * (2 * kStages + 5) + 4);
+  auto tfull_bar = [&](int a, int sl) { return bar0 + 8u * (2 * kStages + a * SLABS + sl); };
+  auto tempty_bar = [&](int a, int sl) {
+    return bar0 + 8u * (2 * kStages + 2 * SLABS + a * SLABS + sl);
+  };
+  const uint32_t final_bar = bar0 + 8u * (2 * kStages + 4 * SLABS);
+  auto cload_bar = [&](int w, uint32_t b) {
+    return bar0 + 8u * (2 * kStages + 4 * SLABS + 1 + 2 * w + static_cast<int>(b));
+  };
+  constexpr int kBarSlots = 2 * kStages + 4 * SLABS + 1 + 2 * Cfg::kEpiWarps;
+  static_assert(kBarSlots * 8 + 8 <= Cfg::kBarBytes, "barrier area");
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_area + 8 * kBarSlots);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_area + 8 * kBarSlots + 4);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // position in the CTA pair
+  const bool leader = rank == 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), Cfg::kEpiThreads);
-    }
+    for (int a = 0; a < 2; ++a)
+      for (int sl = 0; sl < SLABS; ++sl) {
+        mbar_init(tfull_bar(a, sl), 1);
+        mbar_init(tempty_bar(a, sl), Cfg::kEpiWarps * (PAIR ? 2 : 1));
+      }
     mbar_init(final_bar, 1);
+    for (int w = 0; w < Cfg::kEpiWarps; ++w) {
+      mbar_init(cload_bar(w, 0), 1);
+      mbar_init(cload_bar(w, 1), 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    if (p.c_tma) tma_prefetch_desc(&tmap_c);
+  }
+  if constexpr (PAIR) {
+    cluster_sync_all();  // peer barriers initialised before any remote arrival
+  } else {
+    __syncthreads();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(smem_u32(tmem_slot), Cfg::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) {
+    cluster_sync_all();
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   const int num_tiles = p.tiles_m * p.tiles_n;
+  const int unit = PAIR ? static_cast<int>(blockIdx.x / 2) : static_cast<int>(blockIdx.x);
+  const int num_units = PAIR ? static_cast<int>(gridDim.x / 2) : static_cast<int>(gridDim.x);
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- TMA producer ----------------
+      // ---------------- TMA producer (every CTA) ----------------
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = unit; t < num_tiles && ok; t += num_units) {
         int tm, tn;
         tile_coords(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
-        const int m0 = tm * Cfg::BM;
-        const int n0 = tn * BN;
+        const int m0 = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kCtaRows;
+        const int n0 = tn * BN + static_cast<int>(rank) * Cfg::kBCols;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag, p.err,
                          kErrTimeoutProducer)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes);
-          tma_load_2d(sA0 + stage * Cfg::kABytes, &tmap_a, full_bar(stage), kb * Cfg::BK, m0);
+          if (leader) mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes * (PAIR ? 2 : 1));
+          const uint32_t fb = PAIR ? mapa_shared(full_bar(stage), 0) : full_bar(stage);
+          tma_load_2d<PAIR>(sA0 + stage * Cfg::kABytes, &tmap_a, fb, kb * Cfg::BK, m0);
+          if constexpr (BKM) {
+            tma_load_2d<PAIR>(sB0 + stage * Cfg::kBBytes, &tmap_b, fb, kb * Cfg::BK, n0);
+          } else {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(sB0 + stage * Cfg::kBBytes + j * Cfg::kBBoxBytes, &tmap_b,
-                        full_bar(stage), n0 + 64 * j, kb * Cfg::BK);
+            for (int j = 0; j < Cfg::kBCols / 64; ++j)
+              tma_load_2d<PAIR>(sB0 + stage * Cfg::kBBytes + j * Cfg::kBBoxBytes, &tmap_b, fb,
+                                n0 + 64 * j, kb * Cfg::BK);
+          }
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -203,24 +310,17 @@ __global__ void __launch_bounds__(TcCfg<BN>::kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- UMMA issuer ----------------
-      constexpr uint32_t idesc = make_idesc_f16(Cfg::BM, BN, /*a_mn_major=*/false,
-                                                /*b_mn_major=*/true);
+    if (lane == 0 && leader) {
+      // ---------------- UMMA issuer (even CTA) ----------------
+      constexpr uint32_t idesc = make_idesc_f16(Cfg::kMmaM, BN, /*a_mn_major=*/false,
+                                                /*b_mn_major=*/!BKM);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, abort_flag, p.err,
-                       kErrTimeoutMma)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+      for (int t = unit; t < num_tiles && ok; t += num_units) {
+        for (int kb = 0; kb < p.num_kb && ok; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, abort_flag, p.err,
                          kErrTimeoutMma)) {
             ok = false;
@@ -230,70 +330,179 @@ __global__ void __launch_bounds__(TcCfg<BN>::kThreads, 1)
           const uint32_t a_addr = sA0 + stage * Cfg::kABytes;
           const uint32_t b_addr = sB0 + stage * Cfg::kBBytes;
 #pragma unroll
-          for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
-            // A: K-major, 128B swizzle; advance 16 K-elements = 32 bytes inside
-            // the swizzle row. SBO = 8 rows * 128 B.
-            const uint64_t adesc = make_smem_desc(a_addr + kk * 32, 16, 1024);
-            // B: MN-major, 128B swizzle; 16 K-rows = two 8-row groups of
-            // 1024 B. LBO = distance between 64-column boxes, SBO = 8 K-rows.
-            const uint64_t bdesc = make_smem_desc(b_addr + kk * 2048, Cfg::kBBoxBytes, 1024);
-            umma_f16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          for (int sl = 0; sl < SLABS; ++sl) {
+            if (kb == 0) {
+              // this slab's accumulator must have been drained by the epilogue
+              if (!mbar_wait(tempty_bar(acc, sl), acc_phase ^ 1u, p.timeout_ns, abort_flag, p.err,
+                             kErrTimeoutMma)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            const uint32_t d_tmem =
+                tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols + sl * BN);
+#pragma unroll
+            for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
+              // A: K-major, 128B swizzle; advance 16 K-elements = 32 bytes
+              // inside the swizzle row. SBO = 8 rows * 128 B.
+              const uint64_t adesc =
+                  make_smem_desc(a_addr + sl * Cfg::kSlabBytes + kk * 32, 16, 1024);
+              // B, N-major: 128B swizzle; 16 K-rows = two 8-row groups of
+              // 1024 B. LBO = distance between 64-column boxes, SBO = 8 K-rows.
+              // B, K-major: laid out like A (rows of 64 K, 32 bytes per K step).
+              const uint64_t bdesc =
+                  BKM ? make_smem_desc(b_addr + kk * 32, 16, 1024)
+                      : make_smem_desc(b_addr + kk * 2048, Cfg::kBBoxBytes, 1024);
+              umma_f16<PAIR>(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            }
+            if (kb == p.num_kb - 1) umma_commit_to<PAIR>(tfull_bar(acc, sl));
           }
-          umma_commit(empty_bar(stage));
+          if (!ok) break;
+          umma_commit_to<PAIR>(empty_bar(stage));
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        if (!ok) break;
-        umma_commit(tfull_bar(acc));
-        if (++acc == 2) {
+        if (++acc == Cfg::kAccBufs) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
       // Drain: all UMMAs issued by this thread complete before TMEM is freed.
-      umma_commit(final_bar);
+      umma_commit_local<PAIR>(final_bar);
       volatile int no_abort = 0;
       mbar_wait(final_bar, 0, p.timeout_ns, &no_abort, p.err, kErrTimeoutMma);
     }
   } else {
-    // ---------------- Epilogue (warps 2..5) ----------------
+    // ---------------- Epilogue (warps 2..5 of every CTA) ----------------
+    const int ew = warp - 2;
     const int quad = warp & 3;  // TMEM lane quadrant accessible by this warp
-    const int row_in_tile = quad * 32 + lane;
+    const bool read_c = p.beta != 0.0f;
+    const uint32_t buf0 = sEpi + static_cast<uint32_t>(ew * 2 * Cfg::kEpiBufBytes);
+    float* lsu_tile = epi_float + ew * 32 * 33;
+    // Chunk c uses staging buffer c & 1 and, when beta != 0, that buffer's
+    // C-load barrier, which completes once per use: parity (c >> 1) & 1.
+    uint32_t chunk_ctr = 0;  // chunks this warp has processed
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+    bool ok = true;
+    constexpr int kChunks = BN / Cfg::kEpiChunk;
+    for (int t = unit; t < num_tiles && ok; t += num_units) {
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
-      if (!mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, abort_flag, p.err,
-                     kErrTimeoutEpilogue))
-        break;
-      tc_fence_after();
-      const int row = tm * Cfg::BM + row_in_tile;
-      const uint32_t t_addr =
-          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      for (int sl = 0; sl < SLABS && ok; ++sl) {
+        const int row_base = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kCtaRows +
+                             sl * Cfg::BM + quad * 32;
+        const int col_base = tn * BN;
+        // Prefetch this slab's first C box while its UMMAs are still running.
+        if (p.c_tma && read_c && lane == 0) {
+          const uint32_t b = chunk_ctr & 1u;
+          bulk_wait_read<0>();  // the buffer's previous TMA store has read it
+          mbar_arrive_expect_tx(cload_bar(ew, b), Cfg::kEpiBufBytes);
+          tma_load_2d<false>(buf0 + b * Cfg::kEpiBufBytes, &tmap_c, cload_bar(ew, b), col_base,
+                             row_base);
+        }
+        if (!mbar_wait(tfull_bar(acc, sl), acc_phase, p.timeout_ns, abort_flag, p.err,
+                       kErrTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                static_cast<uint32_t>(acc * Cfg::kAccCols + sl * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_addr + c * 32, r);
-        tmem_wait_ld();
-        epilogue_store32(p, row, tn * BN + c * 32, r);
+        for (int j = 0; j < kChunks; ++j) {
+          uint32_t r[64];
+          tmem_ld_32x32b_x32(t_addr + j * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+          tmem_ld_32x32b_x32(t_addr + j * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+          tmem_wait_ld();
+          if (j == kChunks - 1) {
+            // the slab's accumulator is in registers: hand TMEM back to the UMMAs
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if constexpr (PAIR)
+                mbar_arrive_cluster(mapa_shared(tempty_bar(acc, sl), 0));
+              else
+                mbar_arrive(tempty_bar(acc, sl));
+            }
+          }
+          const int col0 = col_base + j * Cfg::kEpiChunk;
+          if (p.c_tma) {
+            const uint32_t buf = buf0 + (chunk_ctr & 1u) * Cfg::kEpiBufBytes;
+            // prefetch the next chunk's C box into the other buffer
+            if (read_c && j + 1 < kChunks && lane == 0) {
+              const uint32_t nb = (chunk_ctr + 1) & 1u;
+              bulk_wait_read<0>();  // the other buffer's store (previous chunk) has read it
+              mbar_arrive_expect_tx(cload_bar(ew, nb), Cfg::kEpiBufBytes);
+              tma_load_2d<false>(buf0 + nb * Cfg::kEpiBufBytes, &tmap_c, cload_bar(ew, nb),
+                                 col0 + Cfg::kEpiChunk, row_base);
+            }
+            if (read_c) {
+              if (!mbar_wait(cload_bar(ew, chunk_ctr & 1u), (chunk_ctr >> 1) & 1u, p.timeout_ns,
+                             abort_flag, p.err, kErrTimeoutEpilogue)) {
+                ok = false;
+                break;
+              }
+            } else if (lane == 0) {
+              bulk_wait_read<1>();  // this buffer's store from two chunks ago is done
+            }
+            __syncwarp();
+            // lane = row; 8 swizzled 16-byte pieces of 8 columns each
+            const uint32_t row_addr = buf + static_cast<uint32_t>(lane) * 128u;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const uint32_t addr = row_addr + static_cast<uint32_t>(((q ^ (lane & 7)) * 16));
+              uint4 cv = make_uint4(0, 0, 0, 0);
+              if (read_c) cv = ld_shared_v4(addr);
+              const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
+              uint32_t o[4];
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                const float c0 = read_c ? half_bits_to_float(cw[h] & 0xFFFFu) : 0.0f;
+                const float c1 = read_c ? half_bits_to_float(cw[h] >> 16) : 0.0f;
+                o[h] = pack_half2(fmaf(p.alpha, __uint_as_float(r[8 * q + 2 * h]), p.beta * c0),
+                                  fmaf(p.alpha, __uint_as_float(r[8 * q + 2 * h + 1]), p.beta * c1));
+              }
+              st_shared_v4(addr, make_uint4(o[0], o[1], o[2], o[3]));
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            // a box that starts past the last row or column writes nothing: skip it
+            if (lane == 0 && row_base < p.M && col0 < p.N) {
+              tma_store_2d(&tmap_c, buf, col0, row_base);
+              bulk_commit_group();
+            }
+          } else {
+            epilogue_chunk_lsu(p, lsu_tile, row_base, col0, &r[0], lane);
+            epilogue_chunk_lsu(p, lsu_tile, row_base, col0 + 32, &r[32], lane);
+          }
+          ++chunk_ctr;
+        }
       }
-      tc_fence_before();
-      mbar_arrive(tempty_bar(acc));
-      if (++acc == 2) {
+      if (++acc == Cfg::kAccBufs) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
+    if (lane == 0) bulk_wait_all();  // every TMA store of this warp has landed
   }
 
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  if constexpr (PAIR) {
+    cluster_sync_all();  // no CTA leaves while its peer may still signal it
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
 }
 

@@ -48,6 +48,8 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gemm_selftest_wait_timeout.restype = i
     lib.gemm_launcher_noalloc.argtypes = gemm8 + [vp]
     lib.gemm_launcher_noalloc.restype = i
+    lib.gemm_launcher_tn.argtypes = gemm8 + [vp, i]
+    lib.gemm_launcher_tn.restype = i
     return lib
 
 
@@ -100,6 +102,23 @@ def gemm(a, b, c, alpha: float = 1.0, beta: float = 0.0, stream=None, path: int 
                                   path, tile_n)
         if rc != 0:
             raise GemmError(f"path {path} / tile_n {tile_n} cannot serve M={m} N={n} K={k}")
+
+
+def gemm_tn(a, bt, c, alpha: float = 1.0, beta: float = 0.0, stream=None, tile_n: int = 0) -> None:
+    """C = half(alpha * A @ Bt.T + beta * C) with Bt[N,K] (a linear layer's weight layout)."""
+    lib = load()
+    import torch
+    for name, t in (("A", a), ("Bt", bt), ("C", c)):
+        if t.dtype != torch.float16 or not t.is_cuda or not t.is_contiguous():
+            raise GemmError(f"{name} must be a contiguous CUDA float16 tensor")
+    m, k = a.shape
+    n, k2 = bt.shape
+    if k2 != k or tuple(c.shape) != (m, n):
+        raise GemmError(f"shape mismatch A{tuple(a.shape)} Bt{tuple(bt.shape)} C{tuple(c.shape)}")
+    rc = lib.gemm_launcher_tn(a.data_ptr(), bt.data_ptr(), c.data_ptr(), m, n, k, alpha, beta,
+                              _stream_handle(stream), tile_n)
+    if rc != 0:
+        raise GemmError(f"gemm_launcher_tn refused tile_n={tile_n}")
 
 
 def cublas(a, b, c, alpha: float = 1.0, beta: float = 0.0, stream=None) -> None:

@@ -49,10 +49,23 @@ GEMM_API void gemm_launcher_stream(const gemm_half_t* A, const gemm_half_t* B, g
  * reference, whose kernels are chosen only by src/gemm.cu:18-133).
  * path: 0 = automatic (what gemm_launcher does), 1 = tcgen05 tile kernel,
  * 2 = multi-row streaming kernel (M <= 8), 3 = column kernel (N == 1).
- * tile_n: 0 = automatic, else 64, 128 or 256 for path 1.
+ * tile_n (path 1): 0 = automatic; 64, 128 or 256 = one CTA per 128 x tile_n
+ * output tile (tcgen05.mma.cta_group::1); 2 = a 2-CTA cluster per 256 x 256
+ * output tile (tcgen05.mma.cta_group::2); 3 = a 2-CTA cluster per 512 x 256
+ * output tile (two 128-row A slabs per CTA).
  * Returns 0, or -1 if the forced path cannot serve the shape. */
 GEMM_API int gemm_launcher_ex(const gemm_half_t* A, const gemm_half_t* B, gemm_half_t* C, int M, int N,
                      int K, float alpha, float beta, cudaStream_t stream, int path, int tile_n);
+
+/* C = half_rn(alpha * A * Bt^T + beta * C) with Bt[N,K] row-major: the weight
+ * layout of a linear layer, W[N,K]. The reference has no such entry point; its
+ * TRT-LLM adapter transposes W[N,K] into B[K,N] at load time
+ * (samples/trtllm_gemm/adapter.py:46-51) before calling the NN launcher. Same
+ * arithmetic, edge handling and return codes as gemm_launcher_ex path 1
+ * (tcgen05 kernels with B read K-major); tile_n as for gemm_launcher_ex. */
+GEMM_API int gemm_launcher_tn(const gemm_half_t* A, const gemm_half_t* Bt, gemm_half_t* C, int M,
+                              int N, int K, float alpha, float beta, cudaStream_t stream,
+                              int tile_n);
 
 /* gemm_launcher_stream for callers that cannot let a library allocate device
  * memory. No counterpart in the reference.

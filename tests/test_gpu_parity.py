@@ -47,10 +47,12 @@ def test_sharded_config_one_slab(lib, cuda):
 # Every path, forced, across tile and K-block edges
 # ---------------------------------------------------------------------------
 TC_SHAPES = [(128, 256, 64), (256, 512, 128), (129, 257, 65), (1, 8, 8), (127, 200, 1000),
-             (300, 1000, 72), (1024, 1024, 1024), (640, 384, 4104), (2048, 2048, 64)]
+             (300, 1000, 72), (1024, 1024, 1024), (640, 384, 4104), (2048, 2048, 64),
+             (513, 264, 200), (1000, 2056, 136)]
 
 
-@pytest.mark.parametrize("tile_n", [64, 128, 256])
+@pytest.mark.parametrize("tile_n", [64, 128, 256, 2, 3],
+                         ids=["128x64", "128x128", "128x256", "pair256x256", "pair512x256"])
 @pytest.mark.parametrize("shape", TC_SHAPES, ids=str)
 def test_tc_path(lib, cuda, shape, tile_n):
     m, n, k = shape
@@ -184,7 +186,7 @@ def test_dispatch_choices(lib, cuda):
         run(lib, cuda, *shape, fn="launcher")
         names[shape] = gemm_b200.last_kernel()
     assert names[(1024, 1024, 1024)].startswith("tc_gemm_kernel")
-    assert names[(8192, 8192, 64)].startswith("tc_gemm_kernel<128x256>")
+    assert names[(8192, 8192, 64)].startswith("tc_gemm_kernel<512x256,pair>")
     assert names[(1, 28672, 8192)].startswith("rows_gemv_kernel<1>")
     assert names[(28672, 1, 8192)].startswith("col_gemv_kernel")
     assert names[(3, 5000, 4097)].startswith("rows_gemv_kernel<4>")
