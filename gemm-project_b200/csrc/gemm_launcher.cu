@@ -62,6 +62,7 @@ struct DeviceInfo {
   int sms = 0;
   int pair_clusters = 0;          // co-resident 2-CTA clusters, 256 x 256 pair tiles
   int pair2_clusters = 0;         // co-resident 2-CTA clusters, 512 x 256 pair tiles
+  int pairn_clusters = 0;         // co-resident 2-CTA clusters, 256 x 512 pair tiles
   int* err = nullptr;
   cudaMemPool_t pool = nullptr;   // repack scratch (never trimmed between calls)
   bool configured = false;
@@ -105,23 +106,23 @@ int env_int(const char* name) {
   return v ? std::atoi(v) : 0;
 }
 
-template <int BN, bool PAIR, int SLABS>
+template <int BN, bool PAIR, int SLABS, bool SLAB_N = false>
 void configure_tc() {
-  cudaFuncSetAttribute(tc_gemm_kernel<BN, PAIR, false, SLABS>,
+  cudaFuncSetAttribute(tc_gemm_kernel<BN, PAIR, false, SLABS, SLAB_N>,
                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       TcCfg<BN, PAIR, false, SLABS>::kSmemBytes);
-  cudaFuncSetAttribute(tc_gemm_kernel<BN, PAIR, true, SLABS>,
+                       TcCfg<BN, PAIR, false, SLABS, SLAB_N>::kSmemBytes);
+  cudaFuncSetAttribute(tc_gemm_kernel<BN, PAIR, true, SLABS, SLAB_N>,
                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       TcCfg<BN, PAIR, true, SLABS>::kSmemBytes);
+                       TcCfg<BN, PAIR, true, SLABS, SLAB_N>::kSmemBytes);
 }
 
 // Co-resident 2-CTA clusters of a pair kernel (0 if it cannot be placed).
-template <int SLABS>
+template <int SLABS, bool SLAB_N = false>
 int pair_capacity(int sms) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
-  cfg.blockDim = dim3(TcCfg<256, true, false, SLABS>::kThreads, 1, 1);
-  cfg.dynamicSmemBytes = TcCfg<256, true, false, SLABS>::kSmemBytes;
+  cfg.blockDim = dim3(TcCfg<256, true, false, SLABS, SLAB_N>::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = TcCfg<256, true, false, SLABS, SLAB_N>::kSmemBytes;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
@@ -130,7 +131,7 @@ int pair_capacity(int sms) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<256, true, false, SLABS>, &cfg) !=
+  if (cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<256, true, false, SLABS, SLAB_N>, &cfg) !=
       cudaSuccess) {
     cudaGetLastError();
     n = 0;
@@ -155,8 +156,10 @@ DeviceInfo& device_info() {
     configure_tc<256, false, 1>();
     configure_tc<256, true, 1>();
     configure_tc<256, true, 2>();
+    configure_tc<256, true, 2, true>();
     d.pair_clusters = pair_capacity<1>(d.sms);
     d.pair2_clusters = pair_capacity<2>(d.sms);
+    d.pairn_clusters = pair_capacity<2, true>(d.sms);
     {
       cudaMemPoolProps props{};
       props.allocType = cudaMemAllocationTypePinned;
@@ -197,9 +200,10 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D FP16 tensor map, 128B swizzle, zero fill out of bounds.
+// 2-D FP16 tensor map, zero fill out of bounds (128B swizzle by default).
 bool make_tmap(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
-               uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer) {
+               uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer,
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {inner, outer};
@@ -207,7 +211,7 @@ bool make_tmap(CUtensorMap* map, const void* base, uint64_t inner, uint64_t oute
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -228,13 +232,16 @@ void launch_scale(half* C, int M, int N, float beta, cudaStream_t s, const Devic
 
 // Tile shapes of the tcgen05 path (the `tile_n` codes of gemm_launcher_ex):
 // 64, 128, 256 = one CTA per 128 x tile tile; kTilePair = 256 x 256 per 2-CTA
-// cluster; kTilePair2 = 512 x 256 per 2-CTA cluster (two A slabs per CTA).
+// cluster; kTilePair2 = 512 x 256 per 2-CTA cluster (two A slabs per CTA);
+// kTilePairN = 256 x 512 per 2-CTA cluster (two B tiles per CTA sharing A).
 constexpr int kTilePair = 2;
 constexpr int kTilePair2 = 3;
+constexpr int kTilePairN = 4;
 
 bool tile_available(int tile, const DeviceInfo& d) {
   return tile == 64 || tile == 128 || tile == 256 || (tile == kTilePair && d.pair_clusters > 0) ||
-         (tile == kTilePair2 && d.pair2_clusters > 0);
+         (tile == kTilePair2 && d.pair2_clusters > 0) ||
+         (tile == kTilePairN && d.pairn_clusters > 0);
 }
 
 // Pick the tile that minimises (waves x per-SM tile work / efficiency). The
@@ -248,7 +255,8 @@ int choose_tile(int M, int N, const DeviceInfo& d) {
     float eff;
   };
   // sm_cols: output columns x (rows / 128) one SM computes per tile
-  const Cand cands[5] = {{kTilePair2, 512, 256, d.pair2_clusters, 512, 1.1f},
+  const Cand cands[6] = {{kTilePairN, 256, 512, d.pairn_clusters, 512, 1.12f},
+                         {kTilePair2, 512, 256, d.pair2_clusters, 512, 1.1f},
                          {kTilePair, 256, 256, d.pair_clusters, 256, 1.0f},
                          {256, 128, 256, d.sms, 256, 0.95f},
                          {128, 128, 128, d.sms, 128, 0.8f},
@@ -273,20 +281,23 @@ int raster_group(int tiles_m) {
   return std::max(1, std::min(tiles_m, g > 0 ? g : 8));
 }
 
-template <int BN, bool PAIR, bool BKM, int SLABS>
+template <int BN, bool PAIR, bool BKM, int SLABS, bool SLAB_N = false>
 void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                   const TcParams& p, const DeviceInfo& d, cudaStream_t s, int M, int N, int K) {
-  using Cfg = TcCfg<BN, PAIR, BKM, SLABS>;
+  using Cfg = TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>;
   const int tiles = p.tiles_m * p.tiles_n;
-  static const char* names[2][5] = {
+  static const char* names[2][6] = {
       {"tc_gemm_kernel<128x64>", "tc_gemm_kernel<128x128>", "tc_gemm_kernel<128x256>",
-       "tc_gemm_kernel<256x256,pair>", "tc_gemm_kernel<512x256,pair>"},
+       "tc_gemm_kernel<256x256,pair>", "tc_gemm_kernel<512x256,pair>",
+       "tc_gemm_kernel<256x512,pair>"},
       {"tc_gemm_kernel<128x64,tn>", "tc_gemm_kernel<128x128,tn>", "tc_gemm_kernel<128x256,tn>",
-       "tc_gemm_kernel<256x256,pair,tn>", "tc_gemm_kernel<512x256,pair,tn>"}};
-  const int idx = PAIR ? (SLABS == 2 ? 4 : 3) : (BN == 64 ? 0 : (BN == 128 ? 1 : 2));
+       "tc_gemm_kernel<256x256,pair,tn>", "tc_gemm_kernel<512x256,pair,tn>",
+       "tc_gemm_kernel<256x512,pair,tn>"}};
+  const int idx =
+      PAIR ? (SLAB_N ? 5 : (SLABS == 2 ? 4 : 3)) : (BN == 64 ? 0 : (BN == 128 ? 1 : 2));
   const char* name = names[BKM ? 1 : 0][idx];
   if constexpr (PAIR) {
-    const int cap = SLABS == 2 ? d.pair2_clusters : d.pair_clusters;
+    const int cap = SLAB_N ? d.pairn_clusters : (SLABS == 2 ? d.pair2_clusters : d.pair_clusters);
     const int clusters = std::min(tiles, cap);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
@@ -301,11 +312,13 @@ void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     log_launch(name, M, N, K, cfg.gridDim, cfg.blockDim);
-    record_error(cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, true, BKM, SLABS>, ta, tb, tc, p));
+    record_error(
+        cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, true, BKM, SLABS, SLAB_N>, ta, tb, tc, p));
   } else {
     const int grid = std::min(tiles, d.sms);
     log_launch(name, M, N, K, dim3(grid), dim3(Cfg::kThreads));
-    tc_gemm_kernel<BN, false, BKM, SLABS><<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(ta, tb, tc, p);
+    tc_gemm_kernel<BN, false, BKM, SLABS, SLAB_N>
+        <<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(ta, tb, tc, p);
     record_error(cudaGetLastError());
   }
 }
@@ -316,8 +329,8 @@ void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
 int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half* C, int M, int N,
                    int K, float alpha, float beta, cudaStream_t s, int tile, const DeviceInfo& d,
                    bool b_kmajor = false) {
-  const bool pair = tile == kTilePair || tile == kTilePair2;
-  const int slabs = tile == kTilePair2 ? 2 : 1;
+  const bool pair = tile == kTilePair || tile == kTilePair2 || tile == kTilePairN;
+  const int slabs = tile == kTilePair2 ? 2 : 1;  // A slabs per CTA
   CUtensorMap ta, tb, tc;
   std::memset(&tc, 0, sizeof(tc));
   const uint32_t b_rows = pair ? 128u : static_cast<uint32_t>(tile);
@@ -326,15 +339,16 @@ int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half*
                         : make_tmap(&tb, b_src, N, K, static_cast<uint64_t>(ldb) * 2, 64, 64);
   const bool ok_a =
       make_tmap(&ta, a_src, K, M, static_cast<uint64_t>(lda) * 2, 64, 128u * slabs);
-  // C goes through TMA (32 rows x 64 columns boxes) when it is TMA-addressable.
+  // C goes through TMA (32 x 32 boxes, 64B swizzle) when it is TMA-addressable.
   const int c_tma = aligned16(C) && N % 8 == 0 &&
-                    make_tmap(&tc, C, N, M, static_cast<uint64_t>(N) * 2, 64, 32);
+                    make_tmap(&tc, C, N, M, static_cast<uint64_t>(N) * 2, 32, 32,
+                              CU_TENSOR_MAP_SWIZZLE_64B);
   if (!(ok_a && ok_b)) {
     record_error(cudaErrorInvalidValue);
     return -1;
   }
   const int tile_m = pair ? 256 * slabs : 128;
-  const int tile_n = pair ? 256 : tile;
+  const int tile_n = tile == kTilePairN ? 512 : (pair ? 256 : tile);
   TcParams p{};
   p.C = C;
   p.M = M;
@@ -357,6 +371,7 @@ int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half*
       case 128: launch_tc_bn<128, false, true, 1>(ta, tb, tc, p, d, s, M, N, K); break;
       case kTilePair: launch_tc_bn<256, true, true, 1>(ta, tb, tc, p, d, s, M, N, K); break;
       case kTilePair2: launch_tc_bn<256, true, true, 2>(ta, tb, tc, p, d, s, M, N, K); break;
+      case kTilePairN: launch_tc_bn<256, true, true, 2, true>(ta, tb, tc, p, d, s, M, N, K); break;
       default: launch_tc_bn<256, false, true, 1>(ta, tb, tc, p, d, s, M, N, K); break;
     }
   } else {
@@ -365,6 +380,7 @@ int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half*
       case 128: launch_tc_bn<128, false, false, 1>(ta, tb, tc, p, d, s, M, N, K); break;
       case kTilePair: launch_tc_bn<256, true, false, 1>(ta, tb, tc, p, d, s, M, N, K); break;
       case kTilePair2: launch_tc_bn<256, true, false, 2>(ta, tb, tc, p, d, s, M, N, K); break;
+      case kTilePairN: launch_tc_bn<256, true, false, 2, true>(ta, tb, tc, p, d, s, M, N, K); break;
       default: launch_tc_bn<256, false, false, 1>(ta, tb, tc, p, d, s, M, N, K); break;
     }
   }
@@ -541,7 +557,7 @@ int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float a
     return 0;
   }
   if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256 && tile_n != kTilePair &&
-      tile_n != kTilePair2)
+      tile_n != kTilePair2 && tile_n != kTilePairN)
     return -1;
   if (path == 0) {
     if (M <= 8)
@@ -722,7 +738,7 @@ extern "C" GEMM_API int gemm_launcher_tn(const half* A, const half* Bt, half* C,
                                          int K, float alpha, float beta, cudaStream_t stream,
                                          int tile_n) {
   if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256 && tile_n != kTilePair &&
-      tile_n != kTilePair2)
+      tile_n != kTilePair2 && tile_n != kTilePairN)
     return -1;
   return launch_tn(A, Bt, C, M, N, K, alpha, beta, stream, tile_n);
 }

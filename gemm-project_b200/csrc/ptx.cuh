@@ -37,6 +37,17 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// One lane of the (fully active) warp is elected; returns true on that lane.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ uint32_t lane_id() {
   uint32_t l;
   asm volatile("mov.u32 %0, %%laneid;" : "=r"(l));
@@ -101,6 +112,16 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_
       }
     }
   }
+}
+
+// mbar_wait executed by every lane of a warp, with the outcome agreed across
+// the warp, so that a timeout on any lane makes the whole warp unwind together
+// (the warp-collective tcgen05 and elect.sync instructions that follow need
+// every lane).
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, uint64_t timeout_ns,
+                                               volatile int* abort_flag, int* err, int code) {
+  const bool ok = mbar_wait(bar, parity, timeout_ns, abort_flag, err, code);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // ---------------------------------------------------------------------------
@@ -222,25 +243,28 @@ __device__ __forceinline__ void tc_fence_after() {
 // D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16 (FP16 inputs, FP32
 // accumulate). PAIR = cta_group::2: one thread of the even CTA drives both
 // CTAs' tensor cores; A rows and B columns come half from each CTA's smem.
-template <bool PAIR>
+// COLLECT: 0 = plain; 1 = collector::a::fill (read A and keep it in the A
+// collector buffer); 2 = collector::a::lastuse (take A from the collector,
+// the same a-desc as the preceding fill, and release it).
+#define GEMM_B200_UMMA(CG, COLL)                                                          \
+  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"                       \
+               "tcgen05.mma.cta_group::" CG ".kind::f16" COLL " [%0], %1, %2, %3, p;\n\t}" \
+               ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)       \
+               : "memory")
+template <bool PAIR, int COLLECT = 0>
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {
   if constexpr (PAIR) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
+    if constexpr (COLLECT == 1) GEMM_B200_UMMA("2", ".collector::a::fill");
+    else if constexpr (COLLECT == 2) GEMM_B200_UMMA("2", ".collector::a::lastuse");
+    else GEMM_B200_UMMA("2", "");
   } else {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
+    if constexpr (COLLECT == 1) GEMM_B200_UMMA("1", ".collector::a::fill");
+    else if constexpr (COLLECT == 2) GEMM_B200_UMMA("1", ".collector::a::lastuse");
+    else GEMM_B200_UMMA("1", "");
   }
 }
+#undef GEMM_B200_UMMA
 
 // Arrive (once) on the mbarrier at shared::cluster address `bar` when all
 // UMMAs previously issued by this thread have completed.

@@ -24,7 +24,7 @@
 // the two slabs fill TMEM and are released one at a time, so the drain of a
 // slab overlaps the next tile's first UMMAs of the other slab.
 //
-// Roles (192 threads per CTA, grid-stride over tiles, grouped raster):
+// Roles (320 threads per CTA, grid-stride over tiles, grouped raster):
 //   warp 0        TMA producer: one lane streams A (rows x 64) and B boxes into
 //                 a kStages-deep ring of 128B-swizzled smem stages. A stage's
 //                 `full` mbarrier (in the pair's even CTA) counts the bytes of
@@ -33,14 +33,14 @@
 //                 each, four per 64-wide stage and slab), frees stages with
 //                 tcgen05.commit -> `empty[s]` of both CTAs and publishes each
 //                 finished slab with tcgen05.commit -> `tmem_full` of both CTAs.
-//   warps 2..5    epilogue, one TMEM lane quadrant each: tcgen05.ld 32 rows x
-//                 64 columns, alpha/beta in FP32, round to half. When C is
+//   warps 2..9    epilogue, two per TMEM lane quadrant (each half of the
+//                 columns): tcgen05.ld its whole share of a finished slab, release
+//                 the accumulator at once, then alpha/beta in FP32, round to half. When C is
 //                 TMA-addressable: C box TMA-loaded into a 128B-swizzled staging
 //                 tile (beta != 0), result written back there, TMA-stored (out-
 //                 of-range rows/columns are clipped by the hardware). Otherwise:
 //                 transpose through a padded smem tile, per-element predicated
-//                 stores. The slab's accumulator is released right after its
-//                 last tcgen05.ld.
+//                 stores.
 // No TMA load uses cluster multicast, and no operand is another GPU's memory.
 // Every mbarrier wait is bounded (ptx.cuh mbar_wait): on expiry the kernel
 // records an error code and unwinds; it never traps.
@@ -50,30 +50,45 @@
 
 namespace gemm_b200 {
 
-template <int BN_, bool PAIR_, bool BKM_ = false, int SLABS_ = 1>
+template <int BN_, bool PAIR_, bool BKM_ = false, int SLABS_ = 1, bool SLAB_N_ = false>
 struct TcCfg {
   static constexpr bool kPair = PAIR_;
   static constexpr bool kBKMajor = BKM_;                // B given as Bt[N,K]
-  static constexpr int kSlabs = SLABS_;                 // 128-row A slabs per CTA
-  static constexpr int BM = 128;                        // rows per slab
-  static constexpr int BN = BN_;                        // output columns per tile
+  static constexpr int kSlabs = SLABS_;                 // accumulator slabs per CTA
+  // Slabs stack along M (two 128-row A slabs sharing the B tile) or, with
+  // SLAB_N, along N (two B tiles sharing the A slab: consecutive UMMAs reuse A
+  // through the tensor core's A collector buffer).
+  static constexpr bool kSlabN = SLAB_N_;
+  static constexpr int kSlabsM = kSlabN ? 1 : kSlabs;
+  static constexpr int kSlabsN = kSlabN ? kSlabs : 1;
+  static constexpr int BM = 128;                        // rows per M slab
+  static constexpr int BN = BN_;                        // output columns per N slab
   static constexpr int kMmaM = kPair ? 256 : 128;       // M of one UMMA
-  static constexpr int kCtaRows = BM * kSlabs;          // output rows per CTA
+  static constexpr int kCtaRows = BM * kSlabsM;         // output rows per CTA
   static constexpr int kTileM = kCtaRows * (kPair ? 2 : 1);
-  static constexpr int kBCols = kPair ? BN / 2 : BN;    // B columns held by one CTA
+  static constexpr int kTileN = BN * kSlabsN;           // output columns per tile
+  static constexpr int kBCols = kPair ? BN / 2 : BN;    // B columns of one N slab in one CTA
   static constexpr int BK = 64;                         // one 128-byte swizzle row of FP16
-  static constexpr int kSlabBytes = BM * BK * 2;        // 16 KiB
+  static constexpr int kSlabBytes = BM * BK * 2;        // 16 KiB: one A slab
   static constexpr int kABytes = kCtaRows * BK * 2;
   // B boxes: N-major B as 64(N) x 64(K) boxes of 8 KiB; K-major B as one box
   // of kBCols rows x 64 K.
   static constexpr int kBBoxBytes = BKM_ ? kBCols * BK * 2 : 64 * BK * 2;
-  static constexpr int kBBytes = kBCols * BK * 2;
+  static constexpr int kBSlabBytes = kBCols * BK * 2;   // B tile of one N slab
+  static constexpr int kBBytes = kBSlabBytes * kSlabsN;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kEpiWarps = 4;
-  static constexpr int kEpiChunk = 64;                  // columns per epilogue chunk
-  static constexpr int kEpiBufBytes = 32 * kEpiChunk * 2;           // 32 rows x 128 B
-  static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;   // double-buffered
-  static constexpr int kBarBytes = 256;
+  // Epilogue: two warps per TMEM lane quadrant, each owning half of the tile's
+  // columns; C moves through 32 x 32 boxes (64-byte rows, 64B swizzle),
+  // double-buffered per warp.
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kEpiCols = BN / 2;               // columns per epilogue warp per slab
+  static constexpr int kEpiChunk = 32;                  // columns per epilogue chunk
+  static constexpr int kEpiChunks = kEpiCols / kEpiChunk;
+  static constexpr int kEpiBufBytes = 32 * kEpiChunk * 2;           // 2 KiB
+  static constexpr int kEpiTmaBytes = kEpiWarps * 2 * kEpiBufBytes;
+  static constexpr int kEpiLsuBytes = kEpiWarps * 32 * 33 * 4;     // transposed-store fallback
+  static constexpr int kEpiBytes = kEpiTmaBytes > kEpiLsuBytes ? kEpiTmaBytes : kEpiLsuBytes;
+  static constexpr int kBarBytes = 384;
   static constexpr int kSmemLimit = 227 * 1024;
   static constexpr int kStagesFit = (kSmemLimit - kEpiBytes - kBarBytes - 1024) / kStageBytes;
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
@@ -81,15 +96,15 @@ struct TcCfg {
   static constexpr int kAccBufs = 512 / kAccCols >= 2 ? 2 : 1;
   static constexpr int kTmemCols = kAccBufs * kAccCols < 32 ? 32 : kAccBufs * kAccCols;
   static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + kBarBytes + 1024;
-  static constexpr int kThreads = 192;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, MMA, epilogue warps
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
   static_assert(!kPair || BN == 256, "the CTA pair runs 256-column tiles");
   static_assert(kSlabs == 1 || (kSlabs == 2 && kPair), "two slabs only for the CTA pair");
+  static_assert(!kSlabN || kSlabs == 2, "N slabs come in pairs");
   static_assert(kStages >= 3, "pipeline depth");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
   static_assert(kTmemCols <= 512, "TMEM columns");
-  // transposed-store fallback uses 32 x 33 floats per warp inside the staging area
-  static_assert(kEpiWarps * 32 * 33 * 4 <= kEpiBytes, "fallback staging fits");
+  static_assert(kEpiChunks >= 1, "epilogue chunking");
 };
 
 struct TcParams {
@@ -184,12 +199,12 @@ __device__ __forceinline__ void epilogue_chunk_lsu(const TcParams& p, float* til
   __syncwarp();
 }
 
-template <int BN, bool PAIR, bool BKM, int SLABS>
-__global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS>::kThreads, 1)
+template <int BN, bool PAIR, bool BKM, int SLABS, bool SLAB_N>
+__global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_c, const TcParams p) {
-  using Cfg = TcCfg<BN, PAIR, BKM, SLABS>;
+  using Cfg = TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>;
   constexpr int kStages = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
 
@@ -218,6 +233,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS>::kThreads, 1)
   };
   constexpr int kBarSlots = 2 * kStages + 4 * SLABS + 1 + 2 * Cfg::kEpiWarps;
   static_assert(kBarSlots * 8 + 8 <= Cfg::kBarBytes, "barrier area");
+  static_assert((Cfg::kEpiBytes % 8) == 0, "barrier alignment");
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_area + 8 * kBarSlots);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_area + 8 * kBarSlots + 4);
 
@@ -284,7 +300,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS>::kThreads, 1)
         int tm, tn;
         tile_coords(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
         const int m0 = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kCtaRows;
-        const int n0 = tn * BN + static_cast<int>(rank) * Cfg::kBCols;
+        const int n0 = tn * Cfg::kTileN + static_cast<int>(rank) * Cfg::kBCols;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag, p.err,
                          kErrTimeoutProducer)) {
@@ -294,13 +310,18 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS>::kThreads, 1)
           if (leader) mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes * (PAIR ? 2 : 1));
           const uint32_t fb = PAIR ? mapa_shared(full_bar(stage), 0) : full_bar(stage);
           tma_load_2d<PAIR>(sA0 + stage * Cfg::kABytes, &tmap_a, fb, kb * Cfg::BK, m0);
-          if constexpr (BKM) {
-            tma_load_2d<PAIR>(sB0 + stage * Cfg::kBBytes, &tmap_b, fb, kb * Cfg::BK, n0);
-          } else {
 #pragma unroll
-            for (int j = 0; j < Cfg::kBCols / 64; ++j)
-              tma_load_2d<PAIR>(sB0 + stage * Cfg::kBBytes + j * Cfg::kBBoxBytes, &tmap_b, fb,
-                                n0 + 64 * j, kb * Cfg::BK);
+          for (int h = 0; h < Cfg::kSlabsN; ++h) {
+            const uint32_t sb = sB0 + stage * Cfg::kBBytes + h * Cfg::kBSlabBytes;
+            const int nh = n0 + h * BN;
+            if constexpr (BKM) {
+              tma_load_2d<PAIR>(sb, &tmap_b, fb, kb * Cfg::BK, nh);
+            } else {
+#pragma unroll
+              for (int j = 0; j < Cfg::kBCols / 64; ++j)
+                tma_load_2d<PAIR>(sb + j * Cfg::kBBoxBytes, &tmap_b, fb, nh + 64 * j,
+                                  kb * Cfg::BK);
+            }
           }
           if (++stage == kStages) {
             stage = 0;
@@ -310,8 +331,10 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS>::kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && leader) {
+    if (leader) {
       // ---------------- UMMA issuer (even CTA) ----------------
+      // The whole warp runs this loop so that descriptors and TMEM addresses
+      // stay warp-uniform; one elected lane issues each tcgen05 instruction.
       constexpr uint32_t idesc = make_idesc_f16(Cfg::kMmaM, BN, /*a_mn_major=*/false,
                                                 /*b_mn_major=*/!BKM);
       int stage = 0;
@@ -321,45 +344,89 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS>::kThreads, 1)
       bool ok = true;
       for (int t = unit; t < num_tiles && ok; t += num_units) {
         for (int kb = 0; kb < p.num_kb && ok; ++kb) {
-          if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, abort_flag, p.err,
-                         kErrTimeoutMma)) {
+          if (!mbar_wait_warp(full_bar(stage), phase, p.timeout_ns, abort_flag, p.err,
+                              kErrTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_addr = sA0 + stage * Cfg::kABytes;
           const uint32_t b_addr = sB0 + stage * Cfg::kBBytes;
-#pragma unroll
-          for (int sl = 0; sl < SLABS; ++sl) {
+          if constexpr (SLAB_N) {
+            // Both N slabs take the same A: fill the A collector on slab 0 and
+            // reuse it on slab 1. Both accumulators must be free before kb 0.
             if (kb == 0) {
-              // this slab's accumulator must have been drained by the epilogue
-              if (!mbar_wait(tempty_bar(acc, sl), acc_phase ^ 1u, p.timeout_ns, abort_flag, p.err,
-                             kErrTimeoutMma)) {
-                ok = false;
-                break;
-              }
+#pragma unroll
+              for (int sl = 0; sl < SLABS; ++sl)
+                if (ok && !mbar_wait_warp(tempty_bar(acc, sl), acc_phase ^ 1u, p.timeout_ns,
+                                          abort_flag, p.err, kErrTimeoutMma))
+                  ok = false;
+              if (!ok) break;
               tc_fence_after();
             }
-            const uint32_t d_tmem =
-                tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols + sl * BN);
 #pragma unroll
             for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
-              // A: K-major, 128B swizzle; advance 16 K-elements = 32 bytes
-              // inside the swizzle row. SBO = 8 rows * 128 B.
-              const uint64_t adesc =
-                  make_smem_desc(a_addr + sl * Cfg::kSlabBytes + kk * 32, 16, 1024);
-              // B, N-major: 128B swizzle; 16 K-rows = two 8-row groups of
-              // 1024 B. LBO = distance between 64-column boxes, SBO = 8 K-rows.
-              // B, K-major: laid out like A (rows of 64 K, 32 bytes per K step).
-              const uint64_t bdesc =
-                  BKM ? make_smem_desc(b_addr + kk * 32, 16, 1024)
-                      : make_smem_desc(b_addr + kk * 2048, Cfg::kBBoxBytes, 1024);
-              umma_f16<PAIR>(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+              const uint64_t adesc = make_smem_desc(a_addr + kk * 32, 16, 1024);
+              const uint32_t en = (kb | kk) != 0 ? 1u : 0u;
+              const uint32_t d0 = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
+              const uint64_t b0 = BKM ? make_smem_desc(b_addr + kk * 32, 16, 1024)
+                                      : make_smem_desc(b_addr + kk * 2048, Cfg::kBBoxBytes, 1024);
+              const uint64_t b1 =
+                  BKM ? make_smem_desc(b_addr + Cfg::kBSlabBytes + kk * 32, 16, 1024)
+                      : make_smem_desc(b_addr + Cfg::kBSlabBytes + kk * 2048, Cfg::kBBoxBytes,
+                                       1024);
+              if (elect_one()) {
+                umma_f16<PAIR, 1>(d0, adesc, b0, idesc, en);
+                umma_f16<PAIR, 2>(d0 + BN, adesc, b1, idesc, en);
+              }
+              __syncwarp();
             }
-            if (kb == p.num_kb - 1) umma_commit_to<PAIR>(tfull_bar(acc, sl));
+            if (kb == p.num_kb - 1) {
+              if (elect_one()) {
+#pragma unroll
+                for (int sl = 0; sl < SLABS; ++sl) umma_commit_to<PAIR>(tfull_bar(acc, sl));
+              }
+              __syncwarp();
+            }
+          } else {
+#pragma unroll
+            for (int sl = 0; sl < SLABS; ++sl) {
+              if (kb == 0) {
+                // this slab's accumulator must have been drained by the epilogue
+                if (!mbar_wait_warp(tempty_bar(acc, sl), acc_phase ^ 1u, p.timeout_ns, abort_flag,
+                                    p.err, kErrTimeoutMma)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+              }
+              const uint32_t d_tmem =
+                  tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols + sl * BN);
+#pragma unroll
+              for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
+                // A: K-major, 128B swizzle; advance 16 K-elements = 32 bytes
+                // inside the swizzle row. SBO = 8 rows * 128 B.
+                const uint64_t adesc =
+                    make_smem_desc(a_addr + sl * Cfg::kSlabBytes + kk * 32, 16, 1024);
+                // B, N-major: 128B swizzle; 16 K-rows = two 8-row groups of
+                // 1024 B. LBO = distance between 64-column boxes, SBO = 8 K-rows.
+                // B, K-major: laid out like A (rows of 64 K, 32 bytes per K step).
+                const uint64_t bdesc =
+                    BKM ? make_smem_desc(b_addr + kk * 32, 16, 1024)
+                        : make_smem_desc(b_addr + kk * 2048, Cfg::kBBoxBytes, 1024);
+                if (elect_one())
+                  umma_f16<PAIR>(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+                __syncwarp();
+              }
+              if (kb == p.num_kb - 1) {
+                if (elect_one()) umma_commit_to<PAIR>(tfull_bar(acc, sl));
+                __syncwarp();
+              }
+            }
           }
           if (!ok) break;
-          umma_commit_to<PAIR>(empty_bar(stage));
+          if (elect_one()) umma_commit_to<PAIR>(empty_bar(stage));
+          __syncwarp();
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -370,91 +437,93 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS>::kThreads, 1)
           acc_phase ^= 1u;
         }
       }
-      // Drain: all UMMAs issued by this thread complete before TMEM is freed.
-      umma_commit_local<PAIR>(final_bar);
+      // Drain: all UMMAs issued by the elected lane complete before TMEM is freed.
+      if (elect_one()) umma_commit_local<PAIR>(final_bar);
+      __syncwarp();
       volatile int no_abort = 0;
-      mbar_wait(final_bar, 0, p.timeout_ns, &no_abort, p.err, kErrTimeoutMma);
+      mbar_wait_warp(final_bar, 0, p.timeout_ns, &no_abort, p.err, kErrTimeoutMma);
     }
   } else {
-    // ---------------- Epilogue (warps 2..5 of every CTA) ----------------
+    // ---------------- Epilogue (warps 2..9 of every CTA) ----------------
     const int ew = warp - 2;
-    const int quad = warp & 3;  // TMEM lane quadrant accessible by this warp
+    const int quad = warp & 3;      // TMEM lane quadrant accessible by this warp
+    const int col_half = ew >> 2;   // which half of the tile's columns this warp owns
     const bool read_c = p.beta != 0.0f;
     const uint32_t buf0 = sEpi + static_cast<uint32_t>(ew * 2 * Cfg::kEpiBufBytes);
     float* lsu_tile = epi_float + ew * 32 * 33;
-    // Chunk c uses staging buffer c & 1 and, when beta != 0, that buffer's
-    // C-load barrier, which completes once per use: parity (c >> 1) & 1.
-    uint32_t chunk_ctr = 0;  // chunks this warp has processed
+    // Staging buffer of chunk i (counted over the whole kernel) is i & 1; with
+    // beta != 0 each buffer's C-load barrier completes once per use.
+    uint32_t ctr = 0;
+    uint32_t cwait[2] = {0u, 0u};
+    auto issue_c_load = [&](uint32_t chunk_index, int col, int row) {
+      const uint32_t b = chunk_index & 1u;
+      mbar_arrive_expect_tx(cload_bar(ew, b), Cfg::kEpiBufBytes);
+      tma_load_2d<false>(buf0 + b * Cfg::kEpiBufBytes, &tmap_c, cload_bar(ew, b), col, row);
+    };
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    constexpr int kChunks = BN / Cfg::kEpiChunk;
+    constexpr int kChunks = Cfg::kEpiChunks;
     for (int t = unit; t < num_tiles && ok; t += num_units) {
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
       for (int sl = 0; sl < SLABS && ok; ++sl) {
         const int row_base = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kCtaRows +
-                             sl * Cfg::BM + quad * 32;
-        const int col_base = tn * BN;
-        // Prefetch this slab's first C box while its UMMAs are still running.
+                             (SLAB_N ? 0 : sl * Cfg::BM) + quad * 32;
+        const int col_base =
+            tn * Cfg::kTileN + (SLAB_N ? sl * BN : 0) + col_half * Cfg::kEpiCols;
+        // Prefetch this slab's first two C boxes while its UMMAs still run.
         if (p.c_tma && read_c && lane == 0) {
-          const uint32_t b = chunk_ctr & 1u;
-          bulk_wait_read<0>();  // the buffer's previous TMA store has read it
-          mbar_arrive_expect_tx(cload_bar(ew, b), Cfg::kEpiBufBytes);
-          tma_load_2d<false>(buf0 + b * Cfg::kEpiBufBytes, &tmap_c, cload_bar(ew, b), col_base,
-                             row_base);
+          bulk_wait_read<0>();  // earlier TMA stores have finished reading both buffers
+          issue_c_load(ctr, col_base, row_base);
+          if (kChunks > 1) issue_c_load(ctr + 1, col_base + Cfg::kEpiChunk, row_base);
         }
-        if (!mbar_wait(tfull_bar(acc, sl), acc_phase, p.timeout_ns, abort_flag, p.err,
-                       kErrTimeoutEpilogue)) {
+        if (!mbar_wait_warp(tfull_bar(acc, sl), acc_phase, p.timeout_ns, abort_flag, p.err,
+                            kErrTimeoutEpilogue)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        // Whole share of the slab into registers, then hand TMEM back at once.
+        uint32_t r[Cfg::kEpiCols];
         const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                                static_cast<uint32_t>(acc * Cfg::kAccCols + sl * BN);
-#pragma unroll 1
-        for (int j = 0; j < kChunks; ++j) {
-          uint32_t r[64];
-          tmem_ld_32x32b_x32(t_addr + j * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-          tmem_ld_32x32b_x32(t_addr + j * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-          tmem_wait_ld();
-          if (j == kChunks - 1) {
-            // the slab's accumulator is in registers: hand TMEM back to the UMMAs
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-              if constexpr (PAIR)
-                mbar_arrive_cluster(mapa_shared(tempty_bar(acc, sl), 0));
-              else
-                mbar_arrive(tempty_bar(acc, sl));
-            }
-          }
-          const int col0 = col_base + j * Cfg::kEpiChunk;
+                                static_cast<uint32_t>(acc * Cfg::kAccCols + sl * BN +
+                                                      col_half * Cfg::kEpiCols);
+#pragma unroll
+        for (int i = 0; i < kChunks; ++i)
+          tmem_ld_32x32b_x32(t_addr + i * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * i]));
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (PAIR)
+            mbar_arrive_cluster(mapa_shared(tempty_bar(acc, sl), 0));
+          else
+            mbar_arrive(tempty_bar(acc, sl));
+        }
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) {
+          const int col0 = col_base + c * Cfg::kEpiChunk;
           if (p.c_tma) {
-            const uint32_t buf = buf0 + (chunk_ctr & 1u) * Cfg::kEpiBufBytes;
-            // prefetch the next chunk's C box into the other buffer
-            if (read_c && j + 1 < kChunks && lane == 0) {
-              const uint32_t nb = (chunk_ctr + 1) & 1u;
-              bulk_wait_read<0>();  // the other buffer's store (previous chunk) has read it
-              mbar_arrive_expect_tx(cload_bar(ew, nb), Cfg::kEpiBufBytes);
-              tma_load_2d<false>(buf0 + nb * Cfg::kEpiBufBytes, &tmap_c, cload_bar(ew, nb),
-                                 col0 + Cfg::kEpiChunk, row_base);
-            }
+            const uint32_t b = ctr & 1u;
+            const uint32_t buf = buf0 + b * Cfg::kEpiBufBytes;
             if (read_c) {
-              if (!mbar_wait(cload_bar(ew, chunk_ctr & 1u), (chunk_ctr >> 1) & 1u, p.timeout_ns,
-                             abort_flag, p.err, kErrTimeoutEpilogue)) {
+              if (!mbar_wait_warp(cload_bar(ew, b), cwait[b] & 1u, p.timeout_ns, abort_flag,
+                                  p.err, kErrTimeoutEpilogue)) {
                 ok = false;
                 break;
               }
+              ++cwait[b];
             } else if (lane == 0) {
-              bulk_wait_read<1>();  // this buffer's store from two chunks ago is done
+              bulk_wait_read<1>();  // this buffer's previous store has read it
             }
             __syncwarp();
-            // lane = row; 8 swizzled 16-byte pieces of 8 columns each
-            const uint32_t row_addr = buf + static_cast<uint32_t>(lane) * 128u;
+            // lane = row: four 16-byte pieces of 8 columns, 64B-swizzled rows
+            const uint32_t row_addr = buf + static_cast<uint32_t>(lane) * 64u;
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const uint32_t addr = row_addr + static_cast<uint32_t>(((q ^ (lane & 7)) * 16));
+            for (int q = 0; q < 4; ++q) {
+              const uint32_t addr =
+                  row_addr + static_cast<uint32_t>(((q ^ ((lane >> 1) & 3)) * 16));
               uint4 cv = make_uint4(0, 0, 0, 0);
               if (read_c) cv = ld_shared_v4(addr);
               const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
@@ -463,23 +532,29 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS>::kThreads, 1)
               for (int h = 0; h < 4; ++h) {
                 const float c0 = read_c ? half_bits_to_float(cw[h] & 0xFFFFu) : 0.0f;
                 const float c1 = read_c ? half_bits_to_float(cw[h] >> 16) : 0.0f;
-                o[h] = pack_half2(fmaf(p.alpha, __uint_as_float(r[8 * q + 2 * h]), p.beta * c0),
-                                  fmaf(p.alpha, __uint_as_float(r[8 * q + 2 * h + 1]), p.beta * c1));
+                o[h] = pack_half2(
+                    fmaf(p.alpha, __uint_as_float(r[32 * c + 8 * q + 2 * h]), p.beta * c0),
+                    fmaf(p.alpha, __uint_as_float(r[32 * c + 8 * q + 2 * h + 1]), p.beta * c1));
               }
               st_shared_v4(addr, make_uint4(o[0], o[1], o[2], o[3]));
             }
             fence_proxy_async_smem();
             __syncwarp();
-            // a box that starts past the last row or column writes nothing: skip it
-            if (lane == 0 && row_base < p.M && col0 < p.N) {
-              tma_store_2d(&tmap_c, buf, col0, row_base);
-              bulk_commit_group();
+            if (lane == 0) {
+              // a box that starts past the last row or column writes nothing: skip it
+              if (row_base < p.M && col0 < p.N) {
+                tma_store_2d(&tmap_c, buf, col0, row_base);
+                bulk_commit_group();
+              }
+              if (read_c && c + 2 < kChunks) {
+                bulk_wait_read<0>();  // the store just issued has read this buffer
+                issue_c_load(ctr + 2, col0 + 2 * Cfg::kEpiChunk, row_base);
+              }
             }
           } else {
-            epilogue_chunk_lsu(p, lsu_tile, row_base, col0, &r[0], lane);
-            epilogue_chunk_lsu(p, lsu_tile, row_base, col0 + 32, &r[32], lane);
+            epilogue_chunk_lsu(p, lsu_tile, row_base, col0, &r[32 * c], lane);
           }
-          ++chunk_ctr;
+          ++ctr;
         }
       }
       if (++acc == Cfg::kAccBufs) {

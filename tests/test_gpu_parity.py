@@ -51,8 +51,9 @@ TC_SHAPES = [(128, 256, 64), (256, 512, 128), (129, 257, 65), (1, 8, 8), (127, 2
              (513, 264, 200), (1000, 2056, 136)]
 
 
-@pytest.mark.parametrize("tile_n", [64, 128, 256, 2, 3],
-                         ids=["128x64", "128x128", "128x256", "pair256x256", "pair512x256"])
+@pytest.mark.parametrize("tile_n", [64, 128, 256, 2, 3, 4],
+                         ids=["128x64", "128x128", "128x256", "pair256x256", "pair512x256",
+                              "pair256x512"])
 @pytest.mark.parametrize("shape", TC_SHAPES, ids=str)
 def test_tc_path(lib, cuda, shape, tile_n):
     m, n, k = shape
@@ -186,7 +187,7 @@ def test_dispatch_choices(lib, cuda):
         run(lib, cuda, *shape, fn="launcher")
         names[shape] = gemm_b200.last_kernel()
     assert names[(1024, 1024, 1024)].startswith("tc_gemm_kernel")
-    assert names[(8192, 8192, 64)].startswith("tc_gemm_kernel<512x256,pair>")
+    assert names[(8192, 8192, 64)].startswith("tc_gemm_kernel<2")  # a CTA-pair tile
     assert names[(1, 28672, 8192)].startswith("rows_gemv_kernel<1>")
     assert names[(28672, 1, 8192)].startswith("col_gemv_kernel")
     assert names[(3, 5000, 4097)].startswith("rows_gemv_kernel<4>")

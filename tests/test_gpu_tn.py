@@ -15,7 +15,7 @@ from oracle import oracle
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("tile", [0, 64, 128, 256, 2, 3])
+@pytest.mark.parametrize("tile", [0, 64, 128, 256, 2, 3, 4])
 @pytest.mark.parametrize("shape", [(128, 256, 64), (129, 257, 65), (300, 1000, 72), (1, 8, 8),
                                    (1024, 1024, 1024), (640, 384, 4104), (17, 19, 23)], ids=str)
 @pytest.mark.parametrize("offset,beta", [(0, 0.0), (1, 0.5)])
