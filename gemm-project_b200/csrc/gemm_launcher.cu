@@ -29,6 +29,7 @@
 #include "gemm_b200.h"
 #include "ptx.cuh"
 #include "skinny.cuh"
+#include "stream.cuh"
 #include "tc_gemm.cuh"
 
 namespace gemm_b200 {
@@ -63,6 +64,7 @@ struct DeviceInfo {
   int pair_clusters = 0;          // co-resident 2-CTA clusters, 256 x 256 pair tiles
   int pair2_clusters = 0;         // co-resident 2-CTA clusters, 512 x 256 pair tiles
   int pairn_clusters = 0;         // co-resident 2-CTA clusters, 256 x 512 pair tiles
+  int stream_slots = 0;           // co-resident CTAs of the TMA streaming kernels
   int* err = nullptr;
   cudaMemPool_t pool = nullptr;   // repack scratch (never trimmed between calls)
   bool configured = false;
@@ -160,6 +162,20 @@ DeviceInfo& device_info() {
     d.pair_clusters = pair_capacity<1>(d.sms);
     d.pair2_clusters = pair_capacity<2>(d.sms);
     d.pairn_clusters = pair_capacity<2, true>(d.sms);
+    {
+      cudaFuncSetAttribute(rows_tma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmemBytes);
+      cudaFuncSetAttribute(rows_tma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmemBytes);
+      cudaFuncSetAttribute(rows_tma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmemBytes);
+      cudaFuncSetAttribute(rows_tma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmemBytes);
+      cudaFuncSetAttribute(col_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmemBytes);
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows_tma_kernel<8>, kStreamThreads,
+                                                        kStreamSmemBytes) != cudaSuccess) {
+        cudaGetLastError();
+        per_sm = 0;
+      }
+      d.stream_slots = per_sm * d.sms;
+    }
     {
       cudaMemPoolProps props{};
       props.allocType = cudaMemAllocationTypePinned;
@@ -548,6 +564,102 @@ int launch_col(const half* A, const half* B, half* C, int M, int N, int K, float
   return 0;
 }
 
+// ---------------------------------------------------------------------------
+// TMA-fed streaming kernels (operands TMA-addressable).
+// ---------------------------------------------------------------------------
+bool rows_tma_ok(const half* A, const half* B, int M, int N, int K, const DeviceInfo& d) {
+  return d.stream_slots > 0 && M <= 8 && aligned16(A) && aligned16(B) && K % 8 == 0 && N % 8 == 0;
+}
+
+bool col_tma_ok(const half* A, const half* B, int N, int K, const DeviceInfo& d) {
+  return d.stream_slots > 0 && N == 1 && aligned16(A) && aligned16(B) && K % 8 == 0;
+}
+
+template <int MR>
+void launch_rows_tma_mr(const CUtensorMap& ta, const CUtensorMap& tb, const StreamParams& p,
+                        int strips, cudaStream_t s, int M, int N, int K) {
+  static const char* names[4] = {"rows_tma_kernel<1>", "rows_tma_kernel<2>", "rows_tma_kernel<4>",
+                                 "rows_tma_kernel<8>"};
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(strips, p.ksplit, 1);
+  cfg.blockDim = dim3(kStreamThreads, 1, 1);
+  cfg.dynamicSmemBytes = kStreamSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = p.ksplit;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  log_launch(names[MR == 1 ? 0 : (MR == 2 ? 1 : (MR == 4 ? 2 : 3))], M, N, K, cfg.gridDim,
+             cfg.blockDim);
+  record_error(cudaLaunchKernelEx(&cfg, rows_tma_kernel<MR>, ta, tb, p));
+}
+
+int launch_rows_tma(const half* A, const half* B, half* C, int M, int N, int K, float alpha,
+                    float beta, cudaStream_t s, const DeviceInfo& d) {
+  const int mr = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
+  CUtensorMap ta, tb;
+  if (!(make_tmap(&tb, B, N, K, static_cast<uint64_t>(N) * 2, kStreamCols, kStreamRows,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) &&
+        make_tmap(&ta, A, K, M, static_cast<uint64_t>(K) * 2, kStreamRows, mr,
+                  CU_TENSOR_MAP_SWIZZLE_NONE))) {
+    record_error(cudaErrorInvalidValue);
+    return -1;
+  }
+  const int strips = ceil_div(N, kStreamCols);
+  int ksplit = 1;
+  while (ksplit < 8 && strips * ksplit * 2 <= d.stream_slots && K / (ksplit * 2) >= 256) ksplit *= 2;
+  StreamParams p{};
+  p.C = C;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.ksplit = ksplit;
+  p.kchunk = ceil_div(ceil_div(K, ksplit), kStreamRows) * kStreamRows;
+  p.timeout_ns = wait_timeout_ns();
+  p.err = d.err;
+  switch (mr) {
+    case 1: launch_rows_tma_mr<1>(ta, tb, p, strips, s, M, N, K); break;
+    case 2: launch_rows_tma_mr<2>(ta, tb, p, strips, s, M, N, K); break;
+    case 4: launch_rows_tma_mr<4>(ta, tb, p, strips, s, M, N, K); break;
+    default: launch_rows_tma_mr<8>(ta, tb, p, strips, s, M, N, K); break;
+  }
+  return 0;
+}
+
+int launch_col_tma(const half* A, const half* B, half* C, int M, int K, float alpha, float beta,
+                   cudaStream_t s, const DeviceInfo& d) {
+  CUtensorMap ta, tb;
+  if (!(make_tmap(&ta, A, K, M, static_cast<uint64_t>(K) * 2, kStreamCols, kStreamRows,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) &&
+        make_tmap(&tb, B, K, 1, static_cast<uint64_t>(K) * 2, kStreamCols, 1,
+                  CU_TENSOR_MAP_SWIZZLE_NONE))) {
+    record_error(cudaErrorInvalidValue);
+    return -1;
+  }
+  const int total_blocks = ceil_div(M, kStreamRows);
+  const int per_cta = ceil_div(total_blocks, d.stream_slots);
+  const int grid = ceil_div(total_blocks, per_cta);
+  StreamParams p{};
+  p.C = C;
+  p.M = M;
+  p.N = 1;
+  p.K = K;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.blocks_per_cta = per_cta;
+  p.timeout_ns = wait_timeout_ns();
+  p.err = d.err;
+  log_launch("col_tma_kernel", M, 1, K, dim3(grid), dim3(kStreamThreads));
+  col_tma_kernel<<<grid, kStreamThreads, kStreamSmemBytes, s>>>(ta, tb, p);
+  record_error(cudaGetLastError());
+  return 0;
+}
+
 int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float alpha, float beta,
              cudaStream_t s, int path, int tile_n) {
   if (M <= 0 || N <= 0) return 0;
@@ -569,8 +681,14 @@ int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float a
   }
   switch (path) {
     case 1: return launch_tc(A, B, C, M, N, K, alpha, beta, s, tile_n, d);
-    case 2: return launch_rows(A, B, C, M, N, K, alpha, beta, s, d);
-    case 3: return launch_col(A, B, C, M, N, K, alpha, beta, s, d);
+    case 2:
+      if (rows_tma_ok(A, B, M, N, K, d)) return launch_rows_tma(A, B, C, M, N, K, alpha, beta, s, d);
+      return launch_rows(A, B, C, M, N, K, alpha, beta, s, d);
+    case 3:
+      if (col_tma_ok(A, B, N, K, d)) return launch_col_tma(A, B, C, M, K, alpha, beta, s, d);
+      return launch_col(A, B, C, M, N, K, alpha, beta, s, d);
+    case 4: return launch_rows(A, B, C, M, N, K, alpha, beta, s, d);
+    case 5: return launch_col(A, B, C, M, N, K, alpha, beta, s, d);
     default: return -1;
   }
 }

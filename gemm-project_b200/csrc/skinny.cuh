@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(kSkinnyThreads)
 
   // Reduce the 8 warps' partials: for each row m, column c of the strip is
   // summed by thread c.
-#pragma unroll 1
+#pragma unroll
   for (int m = 0; m < MR; ++m) {
     __syncthreads();
 #pragma unroll

@@ -48,7 +48,10 @@ GEMM_API void gemm_launcher_stream(const gemm_half_t* A, const gemm_half_t* B, g
 /* Kernel-path selection for tests and benchmarks (no counterpart in the
  * reference, whose kernels are chosen only by src/gemm.cu:18-133).
  * path: 0 = automatic (what gemm_launcher does), 1 = tcgen05 tile kernel,
- * 2 = multi-row streaming kernel (M <= 8), 3 = column kernel (N == 1).
+ * 2 = multi-row streaming kernel (M <= 8; TMA-fed when the operands allow),
+ * 3 = column kernel (N == 1; TMA-fed when the operands allow),
+ * 4 = multi-row kernel with per-thread loads, 5 = column kernel with
+ * per-thread loads (the paths misaligned operands take).
  * tile_n (path 1): 0 = automatic; 64, 128 or 256 = one CTA per 128 x tile_n
  * output tile (tcgen05.mma.cta_group::1); 2 = a 2-CTA cluster per 256 x 256
  * output tile (tcgen05.mma.cta_group::2); 3 = a 2-CTA cluster per 512 x 256

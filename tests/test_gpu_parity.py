@@ -16,7 +16,7 @@ from oracle import oracle
 
 pytestmark = pytest.mark.gpu
 
-PATH_TC, PATH_ROWS, PATH_COL = 1, 2, 3
+PATH_TC, PATH_ROWS, PATH_COL, PATH_ROWS_LSU, PATH_COL_LSU = 1, 2, 3, 4, 5
 
 
 def _go(lib, cuda, m, n, k, alpha=1.0, beta=0.0, **kw):
@@ -62,20 +62,23 @@ def test_tc_path(lib, cuda, shape, tile_n):
 
 @pytest.mark.parametrize("shape", [(1, 8, 8), (2, 264, 300), (3, 5000, 4097), (4, 1024, 1025),
                                    (5, 2048, 8192), (8, 6144, 4096), (1, 28672, 8192),
-                                   (7, 131, 515), (1, 1, 9), (6, 24, 20000)], ids=str)
+                                   (7, 131, 515), (1, 1, 9), (6, 24, 20000), (1, 4096, 1024),
+                                   (3, 5000, 4096), (8, 264, 40)], ids=str)
 @pytest.mark.parametrize("offset", [0, 1, 3])
-def test_rows_path(lib, cuda, shape, offset):
+@pytest.mark.parametrize("path", [PATH_ROWS, PATH_ROWS_LSU], ids=["auto", "lsu"])
+def test_rows_path(lib, cuda, shape, offset, path):
     m, n, k = shape
-    _go(lib, cuda, m, n, k, 0.7, -0.3, path=PATH_ROWS, offsets=(offset, offset, offset),
+    _go(lib, cuda, m, n, k, 0.7, -0.3, path=path, offsets=(offset, offset, offset),
         seed=m * 31 + offset)
 
 
 @pytest.mark.parametrize("shape", [(28672, 1, 8192), (9, 1, 8), (1000, 1, 777), (4096, 1, 14336),
-                                   (33, 1, 1)], ids=str)
+                                   (33, 1, 1), (100, 1, 264), (65, 1, 4096)], ids=str)
 @pytest.mark.parametrize("offset", [0, 1])
-def test_col_path(lib, cuda, shape, offset):
+@pytest.mark.parametrize("path", [PATH_COL, PATH_COL_LSU], ids=["auto", "lsu"])
+def test_col_path(lib, cuda, shape, offset, path):
     m, n, k = shape
-    _go(lib, cuda, m, n, k, 1.0, 0.25, path=PATH_COL, offsets=(offset, offset, offset), seed=m)
+    _go(lib, cuda, m, n, k, 1.0, 0.25, path=path, offsets=(offset, offset, offset), seed=m)
 
 
 # ---------------------------------------------------------------------------
@@ -188,6 +191,6 @@ def test_dispatch_choices(lib, cuda):
         names[shape] = gemm_b200.last_kernel()
     assert names[(1024, 1024, 1024)].startswith("tc_gemm_kernel")
     assert names[(8192, 8192, 64)].startswith("tc_gemm_kernel<2")  # a CTA-pair tile
-    assert names[(1, 28672, 8192)].startswith("rows_gemv_kernel<1>")
-    assert names[(28672, 1, 8192)].startswith("col_gemv_kernel")
+    assert names[(1, 28672, 8192)].startswith("rows_tma_kernel<1>")
+    assert names[(28672, 1, 8192)].startswith("col_tma_kernel")
     assert names[(3, 5000, 4097)].startswith("rows_gemv_kernel<4>")
