@@ -283,9 +283,10 @@ def run_single(args, gb, oracle_cfgs, device, pk):
         # the per-rank slab of the sharded config on one GPU, for the scaling comparison
         sl = dict(oracle_cfgs["sharded32768"], m=4096)
         configs["slab4096x32768x16384"] = measure_config(gb, "slab", sl, stream, 3, 2, device)
-        for key in ("gemv_m1", "gemv_n1"):
+        for key, prof in (("gemv_m1", "rows_tma_gemv_m1"), ("gemv_n1", "col_tma_gemv_n1")):
             configs[key]["hbm_frac"] = configs[key]["gbs"] / pk["hbm_gbs"]
             configs[key]["hbm_frac_unit"] = f"of {pk['source']} {pk['hbm_gbs']} GB/s copy"
+            configs[key]["traffic"] = traffic_from_profile(prof)
 
     traffic = traffic_from_profile("tc_gemm_8192")
     tflop_peak = pk["tflops"]
