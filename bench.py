@@ -338,15 +338,26 @@ def run_multi(args, gb, oracle_cfgs, device, pk, rank, world):
         b = (torch.randn((k, n), generator=g, device=device) / math.sqrt(k)).half()
     else:
         b = torch.empty((k, n), device=device, dtype=torch.float16)
+    # NCCL sets up its channels on the first collective: warm it up on a small
+    # buffer so the timed broadcast measures the transfer.
+    warm = torch.zeros(16 << 20, device=device, dtype=torch.float16)
+    dist.broadcast(warm, src=0)
     dist.barrier()
     torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    dist.broadcast(b, src=0)
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    bcast_ms = torch.tensor([ev0.elapsed_time(ev1)], device=device)
-    dist.all_reduce(bcast_ms, op=dist.ReduceOp.MAX)
+    bcast_times = []
+    for _ in range(3):  # the same bytes each time; B is identical after the first
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        dist.broadcast(b, src=0)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([ev0.elapsed_time(ev1)], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        bcast_times.append(float(t.item()))
+    bcast_ms = torch.tensor([min(bcast_times)], device=device)
+    del warm
     # this rank's A slab (seed = rank) and C slab (zero)
     g = torch.Generator(device=device).manual_seed(1 + rank)
     a = (torch.randn((slab_m, k), generator=g, device=device) / math.sqrt(k)).half()
@@ -411,7 +422,9 @@ def run_multi(args, gb, oracle_cfgs, device, pk, rank, world):
                      "traffic": traffic_from_profile("tc_gemm_8192"),
                      "peak_source": f"{pk['source']} cuBLAS bf16 burst, per GPU"},
         "broadcast": {"bytes": k * n * 2, "ms_max_over_ranks": round(float(bcast_ms.item()), 3),
-                      "gbs": round(k * n * 2 / float(bcast_ms.item()) / 1e6, 1)},
+                      "gbs": round(k * n * 2 / float(bcast_ms.item()) / 1e6, 1),
+                      "note": "one-time replication of B (NCCL over NVLink), best of 3 after a "
+                              "warm-up collective; not inside a step"},
         "e2e": {"value": round(flops_total / e2e_ms / 1e9, 3), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": (a.numel() + c.numel()) * 2 * world,
@@ -522,7 +535,7 @@ def main():
     if world > 1:
         import torch.distributed as dist
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
         out = run_multi(args, gb, CONFIGS, device, pk, rank, world)
         dist.barrier()
         dist.destroy_process_group()
