@@ -7,9 +7,11 @@
 // and pointer alignment, src/gemm.cu:20-24 and :112-133) but routes to sm_100a
 // kernels:
 //   K <= 0                      -> scale_c_kernel (C = beta*C)
-//   M <= 8                      -> rows_gemv_kernel<MR>  (HBM streaming, cluster split-K)
-//   N == 1                      -> col_gemv_kernel       (HBM streaming)
-//   otherwise                   -> tc_gemm_kernel<BN>    (tcgen05 + TMA + TMEM)
+//   M == 1                      -> rows_tma_kernel<1>    (TMA-fed HBM streaming, cluster split-K)
+//   2 <= M <= 64, TMA-friendly  -> skinny_tc_kernel<NM>  (tcgen05, C^T = B^T A^T, cluster split-K)
+//   M <= 8 otherwise            -> rows_gemv_kernel<MR>  (per-thread loads, any alignment)
+//   N == 1                      -> col_tma_kernel / col_gemv_kernel
+//   otherwise                   -> tc_gemm_kernel<...>   (tcgen05 + TMA + TMEM tiles)
 // The tcgen05 path needs TMA-addressable operands (16-byte aligned base, row
 // pitch a multiple of 16 bytes). An operand that is not (K % 8 != 0, N % 8 != 0
 // or a base offset by one half, the reference's misaligned cases) is first
@@ -30,6 +32,7 @@
 #include "ptx.cuh"
 #include "skinny.cuh"
 #include "stream.cuh"
+#include "decode.cuh"
 #include "tc_gemm.cuh"
 
 namespace gemm_b200 {
@@ -65,6 +68,7 @@ struct DeviceInfo {
   int pair2_clusters = 0;         // co-resident 2-CTA clusters, 512 x 256 pair tiles
   int pairn_clusters = 0;         // co-resident 2-CTA clusters, 256 x 512 pair tiles
   int stream_slots = 0;           // co-resident CTAs of the TMA streaming kernels
+  int dec_slots[3] = {0, 0, 0};   // co-resident CTAs of skinny_tc_kernel<16|32|64>
   int* err = nullptr;
   cudaMemPool_t pool = nullptr;   // repack scratch (never trimmed between calls)
   bool configured = false;
@@ -177,6 +181,25 @@ DeviceInfo& device_info() {
       d.stream_slots = per_sm * d.sms;
     }
     {
+      cudaFuncSetAttribute(skinny_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           DecCfg<16>::kSmemBytes);
+      cudaFuncSetAttribute(skinny_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           DecCfg<32>::kSmemBytes);
+      cudaFuncSetAttribute(skinny_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           DecCfg<64>::kSmemBytes);
+      // Capacity from the shared-memory budget (228 KiB per SM, 1 KiB reserved
+      // per CTA), at most two CTAs per SM: the occupancy query reports one CTA
+      // per SM for these TMEM-allocating kernels, while two co-resident CTAs
+      // (32 or 64 TMEM columns each) measure faster.
+      auto slots = [&](int smem) {
+        const int per_sm = std::min(2, (228 * 1024) / (smem + 1024));
+        return per_sm * d.sms;
+      };
+      d.dec_slots[0] = slots(DecCfg<16>::kSmemBytes);
+      d.dec_slots[1] = slots(DecCfg<32>::kSmemBytes);
+      d.dec_slots[2] = slots(DecCfg<64>::kSmemBytes);
+    }
+    {
       cudaMemPoolProps props{};
       props.allocType = cudaMemAllocationTypePinned;
       props.location.type = cudaMemLocationTypeDevice;
@@ -188,6 +211,13 @@ DeviceInfo& device_info() {
         cudaGetLastError();
         d.pool = nullptr;
       }
+    }
+    if (env_int("GEMM_DEBUG_INFO")) {
+      std::fprintf(stderr,
+                   "gemm_b200 device %d: sms=%d pair_clusters=%d pair2_clusters=%d "
+                   "pairn_clusters=%d stream_slots=%d dec_slots=%d/%d/%d\n",
+                   dev, d.sms, d.pair_clusters, d.pair2_clusters, d.pairn_clusters,
+                   d.stream_slots, d.dec_slots[0], d.dec_slots[1], d.dec_slots[2]);
     }
     std::atomic_thread_fence(std::memory_order_release);
     d.configured = true;
@@ -660,6 +690,69 @@ int launch_col_tma(const half* A, const half* B, half* C, int M, int K, float al
   return 0;
 }
 
+// ---------------------------------------------------------------------------
+// Small-M tensor-core path (2 <= M <= 64, TMA-addressable operands).
+// ---------------------------------------------------------------------------
+bool dec_ok(const half* A, const half* B, int M, int N, int K, const DeviceInfo& d) {
+  return d.dec_slots[0] > 0 && M >= 1 && M <= 64 && aligned16(A) && aligned16(B) && K % 8 == 0 &&
+         N % 8 == 0;
+}
+
+template <int NM>
+void launch_dec_nm(const CUtensorMap& ta, const CUtensorMap& tb, const DecParams& p, int tiles,
+                   cudaStream_t s, int M, int N, int K) {
+  static const char* names[3] = {"skinny_tc_kernel<16>", "skinny_tc_kernel<32>",
+                                 "skinny_tc_kernel<64>"};
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(tiles, p.ksplit, 1);
+  cfg.blockDim = dim3(DecCfg<NM>::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = DecCfg<NM>::kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = p.ksplit;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  log_launch(names[NM == 16 ? 0 : (NM == 32 ? 1 : 2)], M, N, K, cfg.gridDim, cfg.blockDim);
+  record_error(cudaLaunchKernelEx(&cfg, skinny_tc_kernel<NM>, ta, tb, p));
+}
+
+int launch_dec(const half* A, const half* B, half* C, int M, int N, int K, float alpha,
+               float beta, cudaStream_t s, const DeviceInfo& d) {
+  const int nm = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+  CUtensorMap ta, tb;
+  if (!(make_tmap(&tb, B, N, K, static_cast<uint64_t>(N) * 2, 64, 64) &&
+        make_tmap(&ta, A, K, M, static_cast<uint64_t>(K) * 2, 64, nm))) {
+    record_error(cudaErrorInvalidValue);
+    return -1;
+  }
+  const int tiles = ceil_div(N, 128);
+  const int slots = d.dec_slots[nm == 16 ? 0 : (nm == 32 ? 1 : 2)];
+  int ksplit = 1;
+  while (ksplit < 8 && tiles * ksplit * 2 <= slots && K / (ksplit * 2) >= 256) ksplit *= 2;
+  const int forced_ks = env_int("GEMM_DEC_KSPLIT");
+  if (forced_ks == 1 || forced_ks == 2 || forced_ks == 4 || forced_ks == 8) ksplit = forced_ks;
+  DecParams p{};
+  p.C = C;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.ksplit = ksplit;
+  p.kchunk = ceil_div(ceil_div(K, ksplit), 64) * 64;
+  p.timeout_ns = wait_timeout_ns();
+  p.err = d.err;
+  switch (nm) {
+    case 16: launch_dec_nm<16>(ta, tb, p, tiles, s, M, N, K); break;
+    case 32: launch_dec_nm<32>(ta, tb, p, tiles, s, M, N, K); break;
+    default: launch_dec_nm<64>(ta, tb, p, tiles, s, M, N, K); break;
+  }
+  return 0;
+}
+
 int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float alpha, float beta,
              cudaStream_t s, int path, int tile_n) {
   if (M <= 0 || N <= 0) return 0;
@@ -672,8 +765,12 @@ int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float a
       tile_n != kTilePair2 && tile_n != kTilePairN)
     return -1;
   if (path == 0) {
-    if (M <= 8)
-      path = 2;
+    if (M == 1)
+      path = 2;                       // streaming GEMV
+    else if (M <= 64 && N > 1 && dec_ok(A, B, M, N, K, d))
+      path = 6;                       // small-M tensor-core kernel
+    else if (M <= 8)
+      path = 2;                       // misaligned small M: per-thread loads
     else if (N == 1)
       path = 3;
     else
@@ -689,6 +786,9 @@ int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float a
       return launch_col(A, B, C, M, N, K, alpha, beta, s, d);
     case 4: return launch_rows(A, B, C, M, N, K, alpha, beta, s, d);
     case 5: return launch_col(A, B, C, M, N, K, alpha, beta, s, d);
+    case 6:
+      if (!dec_ok(A, B, M, N, K, d)) return -1;
+      return launch_dec(A, B, C, M, N, K, alpha, beta, s, d);
     default: return -1;
   }
 }

@@ -16,7 +16,7 @@ from oracle import oracle
 
 pytestmark = pytest.mark.gpu
 
-PATH_TC, PATH_ROWS, PATH_COL, PATH_ROWS_LSU, PATH_COL_LSU = 1, 2, 3, 4, 5
+PATH_TC, PATH_ROWS, PATH_COL, PATH_ROWS_LSU, PATH_COL_LSU, PATH_DEC = 1, 2, 3, 4, 5, 6
 
 
 def _go(lib, cuda, m, n, k, alpha=1.0, beta=0.0, **kw):
@@ -79,6 +79,15 @@ def test_rows_path(lib, cuda, shape, offset, path):
 def test_col_path(lib, cuda, shape, offset, path):
     m, n, k = shape
     _go(lib, cuda, m, n, k, 1.0, 0.25, path=path, offsets=(offset, offset, offset), seed=m)
+
+
+@pytest.mark.parametrize("shape", [(2, 264, 296), (8, 6144, 4096), (16, 1024, 18944), (17, 640, 672),
+                                   (32, 6144, 4096), (33, 2056, 1000), (64, 512, 64), (5, 8, 8),
+                                   (3, 5000, 4096), (48, 4104, 2000), (64, 28672, 8192)], ids=str)
+def test_small_m_tensor_core_path(lib, cuda, shape):
+    m, n, k = shape
+    _go(lib, cuda, m, n, k, 0.75, -0.5, dist="normal", path=PATH_DEC, seed=m + n)
+    _go(lib, cuda, m, n, k, 1.0, 0.0, dist="normal", path=PATH_DEC, seed=m + n + 1)
 
 
 # ---------------------------------------------------------------------------
@@ -194,3 +203,5 @@ def test_dispatch_choices(lib, cuda):
     assert names[(1, 28672, 8192)].startswith("rows_tma_kernel<1>")
     assert names[(28672, 1, 8192)].startswith("col_tma_kernel")
     assert names[(3, 5000, 4097)].startswith("rows_gemv_kernel<4>")
+    run(lib, cuda, 8, 6144, 4096, fn="launcher")
+    assert gemm_b200.last_kernel().startswith("skinny_tc_kernel<16>")
