@@ -506,12 +506,17 @@ int launch_tc(const half* A, const half* B, half* C, int M, int N, int K, float 
   return rc;
 }
 
-template <int MR, bool VEC>
+template <int MR, bool VEC, int TPR>
 void launch_rows_mr(const SkinnyParams& p, int strips, cudaStream_t s, int M, int N, int K) {
-  static const char* names_vec[4] = {"rows_gemv_kernel<1>", "rows_gemv_kernel<2>",
-                                     "rows_gemv_kernel<4>", "rows_gemv_kernel<8>"};
-  static const char* names_sca[4] = {"rows_gemv_kernel<1,scalar>", "rows_gemv_kernel<2,scalar>",
-                                     "rows_gemv_kernel<4,scalar>", "rows_gemv_kernel<8,scalar>"};
+  static const char* names[2][2][4] = {
+      {{"rows_gemv_kernel<1,scalar,half>", "rows_gemv_kernel<2,scalar,half>",
+        "rows_gemv_kernel<4,scalar,half>", "rows_gemv_kernel<8,scalar,half>"},
+       {"rows_gemv_kernel<1,half>", "rows_gemv_kernel<2,half>", "rows_gemv_kernel<4,half>",
+        "rows_gemv_kernel<8,half>"}},
+      {{"rows_gemv_kernel<1,scalar>", "rows_gemv_kernel<2,scalar>", "rows_gemv_kernel<4,scalar>",
+        "rows_gemv_kernel<8,scalar>"},
+       {"rows_gemv_kernel<1>", "rows_gemv_kernel<2>", "rows_gemv_kernel<4>",
+        "rows_gemv_kernel<8>"}}};
   const int idx = MR == 1 ? 0 : (MR == 2 ? 1 : (MR == 4 ? 2 : 3));
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(strips, p.ksplit, 1);
@@ -525,8 +530,17 @@ void launch_rows_mr(const SkinnyParams& p, int strips, cudaStream_t s, int M, in
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  log_launch(VEC ? names_vec[idx] : names_sca[idx], M, N, K, cfg.gridDim, cfg.blockDim);
-  record_error(cudaLaunchKernelEx(&cfg, rows_gemv_kernel<MR, VEC>, p));
+  log_launch(names[TPR == 32 ? 1 : 0][VEC ? 1 : 0][idx], M, N, K, cfg.gridDim, cfg.blockDim);
+  record_error(cudaLaunchKernelEx(&cfg, rows_gemv_kernel<MR, VEC, TPR>, p));
+}
+
+template <int MR, bool VEC>
+void launch_rows_tpr(const SkinnyParams& p, int strips, int tpr, cudaStream_t s, int M, int N,
+                     int K) {
+  if (tpr == 16)
+    launch_rows_mr<MR, VEC, 16>(p, strips, s, M, N, K);
+  else
+    launch_rows_mr<MR, VEC, 32>(p, strips, s, M, N, K);
 }
 
 int launch_rows(const half* A, const half* B, half* C, int M, int N, int K, float alpha,
@@ -545,8 +559,10 @@ int launch_rows(const half* A, const half* B, half* C, int M, int N, int K, floa
   // Element phase of B inside its 16-byte line; identical for every row when N % 8 == 0.
   p.phase = vec ? static_cast<int>((reinterpret_cast<uintptr_t>(B) / 2) % 8) : 0;
   p.groups = ceil_div(N + p.phase, 8);
-  const int strips = ceil_div(p.groups, 32);
   const int target = d.sms * 8;
+  // Narrow matrices: half-warp row segments (128-column strips) for more CTAs.
+  const int tpr = ceil_div(p.groups, 32) * 8 < 2 * d.sms ? 16 : 32;
+  const int strips = ceil_div(p.groups, tpr);
   int ksplit = 1;
   while (ksplit < 8 && strips * ksplit * 2 <= target && K / (ksplit * 2) >= 256) ksplit *= 2;
   p.ksplit = ksplit;
@@ -556,17 +572,17 @@ int launch_rows(const half* A, const half* B, half* C, int M, int N, int K, floa
   const int mr = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
   if (vec) {
     switch (mr) {
-      case 1: launch_rows_mr<1, true>(p, strips, s, M, N, K); break;
-      case 2: launch_rows_mr<2, true>(p, strips, s, M, N, K); break;
-      case 4: launch_rows_mr<4, true>(p, strips, s, M, N, K); break;
-      default: launch_rows_mr<8, true>(p, strips, s, M, N, K); break;
+      case 1: launch_rows_tpr<1, true>(p, strips, tpr, s, M, N, K); break;
+      case 2: launch_rows_tpr<2, true>(p, strips, tpr, s, M, N, K); break;
+      case 4: launch_rows_tpr<4, true>(p, strips, tpr, s, M, N, K); break;
+      default: launch_rows_tpr<8, true>(p, strips, tpr, s, M, N, K); break;
     }
   } else {
     switch (mr) {
-      case 1: launch_rows_mr<1, false>(p, strips, s, M, N, K); break;
-      case 2: launch_rows_mr<2, false>(p, strips, s, M, N, K); break;
-      case 4: launch_rows_mr<4, false>(p, strips, s, M, N, K); break;
-      default: launch_rows_mr<8, false>(p, strips, s, M, N, K); break;
+      case 1: launch_rows_tpr<1, false>(p, strips, tpr, s, M, N, K); break;
+      case 2: launch_rows_tpr<2, false>(p, strips, tpr, s, M, N, K); break;
+      case 4: launch_rows_tpr<4, false>(p, strips, tpr, s, M, N, K); break;
+      default: launch_rows_tpr<8, false>(p, strips, tpr, s, M, N, K); break;
     }
   }
   return 0;

@@ -77,20 +77,28 @@ __device__ __forceinline__ uint4 load_group(const SkinnyParams& p, int k, int co
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// grid = (strips, ksplit); cluster = (1, ksplit, 1). Each CTA covers 256
-// columns (32 groups of 8: lane l of every warp owns group strip*32 + l) and
-// K rows [y*kchunk, (y+1)*kchunk); warp w takes rows w, w+8, ... of that range.
-template <int MR, bool VEC>
+// grid = (strips, ksplit); cluster = (1, ksplit, 1). A CTA covers W = 8*TPR
+// columns: TPR lanes of a warp cover one row segment (16 bytes each, column
+// group strip*TPR + lane % TPR), so a warp reads 32/TPR rows per instruction;
+// TPR = 16 halves the strip width to give narrow matrices more CTAs. K rows
+// [y*kchunk, (y+1)*kchunk) are spread over the 8 warps with 8 loads in flight
+// per thread.
+template <int MR, bool VEC, int TPR>
 __global__ void __launch_bounds__(kSkinnyThreads)
     rows_gemv_kernel(const SkinnyParams p) {
+  constexpr int W = 8 * TPR;                 // strip width (columns)
+  constexpr int RPW = 32 / TPR;              // rows per warp per load step
+  constexpr int RPI = kSkinnyWarps * RPW;    // rows per CTA per load step
   constexpr int kAChunk = SkinnyAChunk<MR>::value;
   __shared__ float sA[MR][kAChunk];
-  __shared__ float sPart[kSkinnyWarps][256 + 1];
-  __shared__ float sSum[MR][256];
+  __shared__ float sPart[kSkinnyWarps][W + 1];
+  __shared__ float sSum[MR][W];
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int group = blockIdx.x * 32 + lane;
+  const int sub = lane / TPR;                // row slot within the warp
+  const int gl = lane % TPR;                 // column group within the strip
+  const int group = blockIdx.x * TPR + gl;
   const int col = group * 8 - p.phase;
   const bool group_valid = group < p.groups;
   const bool full = VEC ? (col >= 0 && col + 8 <= p.N) : false;
@@ -115,18 +123,18 @@ __global__ void __launch_bounds__(kSkinnyThreads)
     }
     __syncthreads();
     if (group_valid) {
-      constexpr int U = 4;
-      int k = warp;
-      for (; k + (U - 1) * kSkinnyWarps < kn; k += U * kSkinnyWarps) {
+      constexpr int U = 8;
+      int k = warp * RPW + sub;
+      for (; k + (U - 1) * RPI < kn; k += U * RPI) {
         uint4 v[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) v[u] = load_group<VEC>(p, kc + k + u * kSkinnyWarps, col, full);
+        for (int u = 0; u < U; ++u) v[u] = load_group<VEC>(p, kc + k + u * RPI, col, full);
 #pragma unroll
         for (int u = 0; u < U; ++u)
 #pragma unroll
-          for (int m = 0; m < MR; ++m) fma_half8(acc[m], sA[m][k + u * kSkinnyWarps], v[u]);
+          for (int m = 0; m < MR; ++m) fma_half8(acc[m], sA[m][k + u * RPI], v[u]);
       }
-      for (; k < kn; k += kSkinnyWarps) {
+      for (; k < kn; k += RPI) {
         const uint4 v = load_group<VEC>(p, kc + k, col, full);
 #pragma unroll
         for (int m = 0; m < MR; ++m) fma_half8(acc[m], sA[m][k], v);
@@ -134,26 +142,38 @@ __global__ void __launch_bounds__(kSkinnyThreads)
     }
   }
 
+  // Rows held by the other half-warp (TPR = 16) belong to the same columns.
+#pragma unroll
+  for (int off = TPR; off < 32; off <<= 1)
+#pragma unroll
+    for (int m = 0; m < MR; ++m)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[m][j] += __shfl_xor_sync(0xFFFFFFFFu, acc[m][j], off);
+
   // Reduce the 8 warps' partials: for each row m, column c of the strip is
   // summed by thread c.
 #pragma unroll
   for (int m = 0; m < MR; ++m) {
     __syncthreads();
+    if (sub == 0) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) sPart[warp][lane * 8 + j] = acc[m][j];
+      for (int j = 0; j < 8; ++j) sPart[warp][gl * 8 + j] = acc[m][j];
+    }
     __syncthreads();
-    float s = 0.0f;
+    if (threadIdx.x < W) {
+      float s = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kSkinnyWarps; ++w) s += sPart[w][threadIdx.x];
-    sSum[m][threadIdx.x] = s;
+      for (int w = 0; w < kSkinnyWarps; ++w) s += sPart[w][threadIdx.x];
+      sSum[m][threadIdx.x] = s;
+    }
   }
   __syncthreads();
 
-  const int strip_col0 = blockIdx.x * 256 - p.phase;
+  const int strip_col0 = blockIdx.x * W - p.phase;
   const bool read_c = p.beta != 0.0f;
   if (p.ksplit == 1) {
-    for (int i = threadIdx.x; i < MR * 256; i += kSkinnyThreads) {
-      const int m = i / 256, c = i % 256;
+    for (int i = threadIdx.x; i < MR * W; i += kSkinnyThreads) {
+      const int m = i / W, c = i % W;
       const int n = strip_col0 + c;
       if (m < p.M && n >= 0 && n < p.N) {
         half* dst = p.C + static_cast<size_t>(m) * p.N + n;
@@ -165,11 +185,11 @@ __global__ void __launch_bounds__(kSkinnyThreads)
   }
 
   // Cluster reduction over the ksplit CTAs that share this strip: rank r
-  // finalizes columns [r*256/ksplit, (r+1)*256/ksplit) of every row.
+  // finalizes columns [r*W/ksplit, (r+1)*W/ksplit) of every row.
   cluster_arrive_release();
   cluster_wait_acquire();
   const int rank = static_cast<int>(cluster_ctarank());
-  const int span = 256 / p.ksplit;
+  const int span = W / p.ksplit;
   for (int i = threadIdx.x; i < MR * span; i += kSkinnyThreads) {
     const int m = i / span, c = rank * span + i % span;
     const uint32_t local = smem_u32(&sSum[m][c]);
