@@ -322,9 +322,12 @@ int choose_tile(int M, int N, const DeviceInfo& d) {
   return best;
 }
 
-int raster_group(int tiles_m) {
+// Raster group for tile_coords: positive = tile-rows per group, negative =
+// tile-columns per group (GEMM_RASTER_GROUP overrides for sweeps).
+int raster_group(int tiles_m, int tiles_n) {
   const int g = env_int("GEMM_RASTER_GROUP");
-  return std::max(1, std::min(tiles_m, g > 0 ? g : 8));
+  if (g < 0) return -std::max(1, std::min(tiles_n, -g));
+  return std::max(1, std::min(tiles_m, g > 0 ? g : 16));
 }
 
 template <int BN, bool PAIR, bool BKM, int SLABS, bool SLAB_N = false>
@@ -406,7 +409,7 @@ int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half*
   p.tiles_m = ceil_div(M, tile_m);
   p.tiles_n = ceil_div(N, tile_n);
   p.num_kb = ceil_div(K, 64);
-  p.group = raster_group(p.tiles_m);
+  p.group = raster_group(p.tiles_m, p.tiles_n);
   p.c_tma = c_tma;
   p.c_vec_ok = aligned16(C) && N % 8 == 0;
   p.timeout_ns = wait_timeout_ns();

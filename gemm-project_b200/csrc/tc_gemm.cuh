@@ -120,17 +120,29 @@ struct TcParams {
   int* err;
 };
 
-// Grouped raster over output tiles: `group` tile-rows advance together along N
-// so that concurrently resident CTAs share A and B tiles in L2.
+// Grouped raster over output tiles so that concurrently resident CTAs share A
+// and B panels in L2. group > 0: `group` tile-rows advance together along N;
+// group < 0: |group| tile-columns advance together along M.
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group, int& tm,
                                             int& tn) {
-  const int per_group = group * tiles_n;
-  const int g = t / per_group;
-  const int first_m = g * group;
-  const int gm = min(tiles_m - first_m, group);
-  const int r = t - g * per_group;
-  tm = first_m + r % gm;
-  tn = r / gm;
+  if (group > 0) {
+    const int per_group = group * tiles_n;
+    const int g = t / per_group;
+    const int first_m = g * group;
+    const int gm = min(tiles_m - first_m, group);
+    const int r = t - g * per_group;
+    tm = first_m + r % gm;
+    tn = r / gm;
+  } else {
+    const int gsz = -group;
+    const int per_group = gsz * tiles_m;
+    const int g = t / per_group;
+    const int first_n = g * gsz;
+    const int gn = min(tiles_n - first_n, gsz);
+    const int r = t - g * per_group;
+    tn = first_n + r % gn;
+    tm = r / gn;
+  }
 }
 
 __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {

@@ -60,6 +60,16 @@ def test_tc_path(lib, cuda, shape, tile_n):
     _go(lib, cuda, m, n, k, 0.75, 0.5, dist="normal", path=PATH_TC, tile_n=tile_n, seed=m + n + k)
 
 
+@pytest.mark.parametrize("group", [1, 3, 64, -1, -3, -64])
+@pytest.mark.parametrize("tile_n", [128, 4], ids=["128x128", "pair256x512"])
+def test_tc_raster_orders(lib, cuda, monkeypatch, group, tile_n):
+    """Every tile is produced exactly once under row- and column-major raster groups,
+    including partial last groups."""
+    monkeypatch.setenv("GEMM_RASTER_GROUP", str(group))
+    _go(lib, cuda, 1300, 2900, 136, 0.75, 0.5, dist="normal", path=PATH_TC, tile_n=tile_n,
+        seed=group + 100)
+
+
 @pytest.mark.parametrize("shape", [(1, 8, 8), (2, 264, 300), (3, 5000, 4097), (4, 1024, 1025),
                                    (5, 2048, 8192), (8, 6144, 4096), (1, 28672, 8192),
                                    (7, 131, 515), (1, 1, 9), (6, 24, 20000), (1, 4096, 1024),
