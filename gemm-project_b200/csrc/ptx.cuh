@@ -75,9 +75,16 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// Arrive on an mbarrier that lives in another CTA of the cluster (address from mapa).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+// Arrive on an mbarrier that lives in another CTA of the cluster (address from
+// mapa) as a pure signal. The release is CTA-scoped: it publishes none of this
+// thread's memory writes to the peer, which makes it far cheaper than a
+// cluster-scope release (measured on B200: about 0.1 us instead of about 1 us,
+// since the cluster-scope form waits for the thread's prior memory operations
+// to become cluster-visible). Used for "TMEM drained" handoffs, whose ordering
+// against the tensor core comes from tcgen05.fence::before_thread_sync on the
+// arriving side and tcgen05.fence::after_thread_sync on the waiting side.
+__device__ __forceinline__ void mbar_arrive_remote_signal(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
                : "memory");
 }
 

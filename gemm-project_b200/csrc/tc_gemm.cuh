@@ -149,9 +149,14 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16)));
 }
 
+// Two FP32 values rounded to nearest-even FP16 and packed (lo in bits 0-15).
+// One packed cvt.rn.f16x2.f32 per pair: the scalar f32->f16 conversion has a
+// fraction of its throughput, which made the epilogue's conversion the critical
+// path between two tiles. Rounding is identical to two cvt.rn.f16.f32.
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  return static_cast<uint32_t>(__half_as_ushort(__float2half_rn(lo))) |
-         (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(hi))) << 16);
+  uint32_t out;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(out) : "f"(hi), "f"(lo));
+  return out;
 }
 
 // ---------------------------------------------------------------------------
@@ -508,8 +513,9 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          if constexpr (PAIR)
-            mbar_arrive_cluster(mapa_shared(tempty_bar(acc, sl), 0));
+          // the even CTA's barrier gates the next tile's UMMAs
+          if (PAIR && !leader)
+            mbar_arrive_remote_signal(mapa_shared(tempty_bar(acc, sl), 0));
           else
             mbar_arrive(tempty_bar(acc, sl));
         }
