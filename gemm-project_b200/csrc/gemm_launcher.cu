@@ -145,6 +145,21 @@ int pair_capacity(int sms) {
   return n;
 }
 
+// The 256x512 tile re-splits its registers with setmaxnreg, and the epilogue
+// warps' larger share is drawn from what the block was launched with. Use the
+// tile only if the compiled kernel's register count covers the split (an inc
+// that cannot be satisfied would wait forever).
+template <bool BKM>
+bool pairn_registers_ok() {
+  using Cfg = TcCfg<256, true, BKM, 2, true>;
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, tc_gemm_kernel<256, true, BKM, 2, true>) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return static_cast<long>(fa.numRegs) * Cfg::kThreads >= Cfg::kRegSplitTotal;
+}
+
 // Per-device one-time set-up: SM count, device error word, kernel attributes.
 DeviceInfo& device_info() {
   int dev = 0;
@@ -165,7 +180,9 @@ DeviceInfo& device_info() {
     configure_tc<256, true, 2, true>();
     d.pair_clusters = pair_capacity<1>(d.sms);
     d.pair2_clusters = pair_capacity<2>(d.sms);
-    d.pairn_clusters = pair_capacity<2, true>(d.sms);
+    d.pairn_clusters = pairn_registers_ok<false>() && pairn_registers_ok<true>()
+                           ? pair_capacity<2, true>(d.sms)
+                           : 0;
     {
       cudaFuncSetAttribute(rows_tma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmemBytes);
       cudaFuncSetAttribute(rows_tma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmemBytes);
@@ -396,6 +413,8 @@ int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half*
     record_error(cudaErrorInvalidValue);
     return -1;
   }
+  // The 256x512 pair kernel moves C through TMA only; same operand maps.
+  if (tile == kTilePairN && !c_tma) tile = kTilePair;
   const int tile_m = pair ? 256 * slabs : 128;
   const int tile_n = tile == kTilePairN ? 512 : (pair ? 256 : tile);
   TcParams p{};

@@ -387,6 +387,21 @@ __device__ __forceinline__ void cluster_sync_all() {
   cluster_wait_acquire();
 }
 
+// Per-warpgroup register re-allocation (all four warps of the warpgroup
+// execute it). inc blocks until the registers are free in the block's pool, so
+// the callers' shares must add up to no more than the block was launched with.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg range");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg range");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---------------------------------------------------------------------------
 // Global loads.
 // ---------------------------------------------------------------------------

@@ -15,16 +15,19 @@
 //   single CTA, 1 slab:  128 x BN per CTA (BN = 64, 128, 256), cta_group::1.
 //   CTA pair,  1 slab:  256 x 256 per 2-CTA cluster, cta_group::2: each CTA
 //                        holds 128 rows of A and 128 of the 256 B columns.
-//   CTA pair,  2 slabs: 512 x 256 per 2-CTA cluster: each CTA holds two
+//   CTA pair,  2 M slabs: 512 x 256 per 2-CTA cluster: each CTA holds two
 //                        128-row A slabs and 128 B columns; per K step two
-//                        UMMAs (one per slab) share the B half, so shared-memory
-//                        and L2 traffic per FLOP drop by a quarter.
+//                        UMMAs (one per slab) share the B half.
+//   CTA pair,  2 N slabs (SLAB_N): 256 x 512 per 2-CTA cluster: each CTA holds
+//                        128 rows of A and two 128-column B halves; per K step
+//                        the slab-0 UMMA fills the tensor core's A collector
+//                        and the slab-1 UMMA reuses it. The large-GEMM tile.
 // The FP32 accumulator lives in TMEM (lane = output row, column = output
-// column); with one slab it is double-buffered across tiles, with two slabs
-// the two slabs fill TMEM and are released one at a time, so the drain of a
-// slab overlaps the next tile's first UMMAs of the other slab.
+// column). With one slab it is double-buffered across tiles; with two slabs
+// they fill TMEM, so the next tile's UMMAs wait until the epilogue has read
+// both slabs out, and the epilogue is built to make that wait short.
 //
-// Roles (320 threads per CTA, grid-stride over tiles, grouped raster):
+// Roles (grid-stride over tiles, grouped raster):
 //   warp 0        TMA producer: one lane streams A (rows x 64) and B boxes into
 //                 a kStages-deep ring of 128B-swizzled smem stages. A stage's
 //                 `full` mbarrier (in the pair's even CTA) counts the bytes of
@@ -33,14 +36,22 @@
 //                 each, four per 64-wide stage and slab), frees stages with
 //                 tcgen05.commit -> `empty[s]` of both CTAs and publishes each
 //                 finished slab with tcgen05.commit -> `tmem_full` of both CTAs.
-//   warps 2..9    epilogue, two per TMEM lane quadrant (each half of the
-//                 columns): tcgen05.ld its whole share of a finished slab, release
-//                 the accumulator at once, then alpha/beta in FP32, round to half. When C is
-//                 TMA-addressable: C box TMA-loaded into a 128B-swizzled staging
-//                 tile (beta != 0), result written back there, TMA-stored (out-
-//                 of-range rows/columns are clipped by the hardware). Otherwise:
-//                 transpose through a padded smem tile, per-element predicated
-//                 stores.
+//   8 epilogue warps (warps 2..9; for SLAB_N warps 4..11 after two idle warps
+//                 that complete warpgroup 0), two per TMEM lane quadrant, each
+//                 owning half of a slab's columns. They tcgen05.ld a finished
+//                 slab share into registers, hand the TMEM back (a CTA-scope
+//                 mbarrier signal to the even CTA), compute alpha*acc + beta*C
+//                 in FP32 and round to half, then write 32 x 32 boxes through
+//                 64B-swizzled staging buffers with TMA stores (out-of-range
+//                 rows/columns are clipped by the hardware).
+//                 Generic tiles: C boxes are TMA-loaded into the staging
+//                 buffers (beta != 0); if C is not TMA-addressable, results are
+//                 transposed through a padded smem tile and stored per element.
+//                 SLAB_N: warpgroup 0 gives registers to the epilogue
+//                 (setmaxnreg 48 / 224), slab 0's C is prefetched into
+//                 registers while the UMMAs run, and between reading slab 0 and
+//                 slab 1 out of TMEM there is only register arithmetic, so the
+//                 next tile starts about a microsecond after this one ends.
 // No TMA load uses cluster multicast, and no operand is another GPU's memory.
 // Every mbarrier wait is bounded (ptx.cuh mbar_wait): on expiry the kernel
 // records an error code and unwinds; it never traps.
@@ -96,7 +107,17 @@ struct TcCfg {
   static constexpr int kAccBufs = 512 / kAccCols >= 2 ? 2 : 1;
   static constexpr int kTmemCols = kAccBufs * kAccCols < 32 ? 32 : kAccBufs * kAccCols;
   static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + kBarBytes + 1024;
-  static constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, MMA, epilogue warps
+  // Warps: producer, UMMA issuer (for the 256x512 tile also two idle warps that
+  // complete warpgroup 0), then the epilogue warps.
+  static constexpr int kEpiWarp0 = kSlabN ? 4 : 2;
+  static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
+  // Register split of the 256x512 tile (setmaxnreg): warpgroup 0 drops to
+  // kRegsCtl per thread, the two epilogue warpgroups rise to kRegsEpi. The
+  // shares must fit in what the block is launched with (kThreads x the
+  // kernel's register count); the launcher checks this before using the tile.
+  static constexpr int kRegsCtl = 48;
+  static constexpr int kRegsEpi = 224;
+  static constexpr int kRegSplitTotal = 128 * kRegsCtl + 32 * kEpiWarps * kRegsEpi;
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
   static_assert(!kPair || BN == 256, "the CTA pair runs 256-column tiles");
   static_assert(kSlabs == 1 || (kSlabs == 2 && kPair), "two slabs only for the CTA pair");
@@ -307,146 +328,390 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
   const int unit = PAIR ? static_cast<int>(blockIdx.x / 2) : static_cast<int>(blockIdx.x);
   const int num_units = PAIR ? static_cast<int>(gridDim.x / 2) : static_cast<int>(gridDim.x);
 
-  if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer (every CTA) ----------------
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int t = unit; t < num_tiles && ok; t += num_units) {
-        int tm, tn;
-        tile_coords(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
-        const int m0 = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kCtaRows;
-        const int n0 = tn * Cfg::kTileN + static_cast<int>(rank) * Cfg::kBCols;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag, p.err,
-                         kErrTimeoutProducer)) {
-            ok = false;
-            break;
-          }
-          if (leader) mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes * (PAIR ? 2 : 1));
-          const uint32_t fb = PAIR ? mapa_shared(full_bar(stage), 0) : full_bar(stage);
-          tma_load_2d<PAIR>(sA0 + stage * Cfg::kABytes, &tmap_a, fb, kb * Cfg::BK, m0);
-#pragma unroll
-          for (int h = 0; h < Cfg::kSlabsN; ++h) {
-            const uint32_t sb = sB0 + stage * Cfg::kBBytes + h * Cfg::kBSlabBytes;
-            const int nh = n0 + h * BN;
-            if constexpr (BKM) {
-              tma_load_2d<PAIR>(sb, &tmap_b, fb, kb * Cfg::BK, nh);
-            } else {
-#pragma unroll
-              for (int j = 0; j < Cfg::kBCols / 64; ++j)
-                tma_load_2d<PAIR>(sb + j * Cfg::kBBoxBytes, &tmap_b, fb, nh + 64 * j,
-                                  kb * Cfg::BK);
+  if (warp < Cfg::kEpiWarp0) {
+    // Control warps (warpgroup 0 for the 256x512 tile): producer, UMMA issuer
+    // and, for that tile, two idle warps; they hand registers to the epilogue.
+    if constexpr (SLAB_N) setmaxnreg_dec<Cfg::kRegsCtl>();
+    if (warp == 0) {
+      if (lane == 0) {
+        // ---------------- TMA producer (every CTA) ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int t = unit; t < num_tiles && ok; t += num_units) {
+          int tm, tn;
+          tile_coords(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
+          const int m0 = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kCtaRows;
+          const int n0 = tn * Cfg::kTileN + static_cast<int>(rank) * Cfg::kBCols;
+          for (int kb = 0; kb < p.num_kb; ++kb) {
+            if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag, p.err,
+                           kErrTimeoutProducer)) {
+              ok = false;
+              break;
             }
-          }
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
+            if (leader) mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes * (PAIR ? 2 : 1));
+            const uint32_t fb = PAIR ? mapa_shared(full_bar(stage), 0) : full_bar(stage);
+            tma_load_2d<PAIR>(sA0 + stage * Cfg::kABytes, &tmap_a, fb, kb * Cfg::BK, m0);
+  #pragma unroll
+            for (int h = 0; h < Cfg::kSlabsN; ++h) {
+              const uint32_t sb = sB0 + stage * Cfg::kBBytes + h * Cfg::kBSlabBytes;
+              const int nh = n0 + h * BN;
+              if constexpr (BKM) {
+                tma_load_2d<PAIR>(sb, &tmap_b, fb, kb * Cfg::BK, nh);
+              } else {
+  #pragma unroll
+                for (int j = 0; j < Cfg::kBCols / 64; ++j)
+                  tma_load_2d<PAIR>(sb + j * Cfg::kBBoxBytes, &tmap_b, fb, nh + 64 * j,
+                                    kb * Cfg::BK);
+              }
+            }
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
         }
       }
+    } else if (warp == 1) {
+      if (leader) {
+        // ---------------- UMMA issuer (even CTA) ----------------
+        // The whole warp runs this loop so that descriptors and TMEM addresses
+        // stay warp-uniform; one elected lane issues each tcgen05 instruction.
+        constexpr uint32_t idesc = make_idesc_f16(Cfg::kMmaM, BN, /*a_mn_major=*/false,
+                                                  /*b_mn_major=*/!BKM);
+        int stage = 0;
+        uint32_t phase = 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        for (int t = unit; t < num_tiles && ok; t += num_units) {
+          for (int kb = 0; kb < p.num_kb && ok; ++kb) {
+            if (!mbar_wait_warp(full_bar(stage), phase, p.timeout_ns, abort_flag, p.err,
+                                kErrTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_addr = sA0 + stage * Cfg::kABytes;
+            const uint32_t b_addr = sB0 + stage * Cfg::kBBytes;
+            if constexpr (SLAB_N) {
+              // Both N slabs take the same A: fill the A collector on slab 0 and
+              // reuse it on slab 1. Both accumulators must be free before kb 0.
+              if (kb == 0) {
+  #pragma unroll
+                for (int sl = 0; sl < SLABS; ++sl)
+                  if (ok && !mbar_wait_warp(tempty_bar(acc, sl), acc_phase ^ 1u, p.timeout_ns,
+                                            abort_flag, p.err, kErrTimeoutMma))
+                    ok = false;
+                if (!ok) break;
+                tc_fence_after();
+              }
+  #pragma unroll
+              for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
+                const uint64_t adesc = make_smem_desc(a_addr + kk * 32, 16, 1024);
+                const uint32_t en = (kb | kk) != 0 ? 1u : 0u;
+                const uint32_t d0 = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
+                const uint64_t b0 = BKM ? make_smem_desc(b_addr + kk * 32, 16, 1024)
+                                        : make_smem_desc(b_addr + kk * 2048, Cfg::kBBoxBytes, 1024);
+                const uint64_t b1 =
+                    BKM ? make_smem_desc(b_addr + Cfg::kBSlabBytes + kk * 32, 16, 1024)
+                        : make_smem_desc(b_addr + Cfg::kBSlabBytes + kk * 2048, Cfg::kBBoxBytes,
+                                         1024);
+                if (elect_one()) {
+                  umma_f16<PAIR, 1>(d0, adesc, b0, idesc, en);
+                  umma_f16<PAIR, 2>(d0 + BN, adesc, b1, idesc, en);
+                }
+                __syncwarp();
+              }
+              if (kb == p.num_kb - 1) {
+                if (elect_one()) {
+  #pragma unroll
+                  for (int sl = 0; sl < SLABS; ++sl) umma_commit_to<PAIR>(tfull_bar(acc, sl));
+                }
+                __syncwarp();
+              }
+            } else {
+  #pragma unroll
+              for (int sl = 0; sl < SLABS; ++sl) {
+                if (kb == 0) {
+                  // this slab's accumulator must have been drained by the epilogue
+                  if (!mbar_wait_warp(tempty_bar(acc, sl), acc_phase ^ 1u, p.timeout_ns, abort_flag,
+                                      p.err, kErrTimeoutMma)) {
+                    ok = false;
+                    break;
+                  }
+                  tc_fence_after();
+                }
+                const uint32_t d_tmem =
+                    tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols + sl * BN);
+  #pragma unroll
+                for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
+                  // A: K-major, 128B swizzle; advance 16 K-elements = 32 bytes
+                  // inside the swizzle row. SBO = 8 rows * 128 B.
+                  const uint64_t adesc =
+                      make_smem_desc(a_addr + sl * Cfg::kSlabBytes + kk * 32, 16, 1024);
+                  // B, N-major: 128B swizzle; 16 K-rows = two 8-row groups of
+                  // 1024 B. LBO = distance between 64-column boxes, SBO = 8 K-rows.
+                  // B, K-major: laid out like A (rows of 64 K, 32 bytes per K step).
+                  const uint64_t bdesc =
+                      BKM ? make_smem_desc(b_addr + kk * 32, 16, 1024)
+                          : make_smem_desc(b_addr + kk * 2048, Cfg::kBBoxBytes, 1024);
+                  if (elect_one())
+                    umma_f16<PAIR>(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+                  __syncwarp();
+                }
+                if (kb == p.num_kb - 1) {
+                  if (elect_one()) umma_commit_to<PAIR>(tfull_bar(acc, sl));
+                  __syncwarp();
+                }
+              }
+            }
+            if (!ok) break;
+            if (elect_one()) umma_commit_to<PAIR>(empty_bar(stage));
+            __syncwarp();
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          if (++acc == Cfg::kAccBufs) {
+            acc = 0;
+            acc_phase ^= 1u;
+          }
+        }
+        // Drain: all UMMAs issued by the elected lane complete before TMEM is freed.
+        if (elect_one()) umma_commit_local<PAIR>(final_bar);
+        __syncwarp();
+        volatile int no_abort = 0;
+        mbar_wait_warp(final_bar, 0, p.timeout_ns, &no_abort, p.err, kErrTimeoutMma);
+      }
     }
-  } else if (warp == 1) {
-    if (leader) {
-      // ---------------- UMMA issuer (even CTA) ----------------
-      // The whole warp runs this loop so that descriptors and TMEM addresses
-      // stay warp-uniform; one elected lane issues each tcgen05 instruction.
-      constexpr uint32_t idesc = make_idesc_f16(Cfg::kMmaM, BN, /*a_mn_major=*/false,
-                                                /*b_mn_major=*/!BKM);
-      int stage = 0;
-      uint32_t phase = 0;
+  } else {
+    // ---------------- Epilogue (the last kEpiWarps warps of every CTA) ----------------
+    if constexpr (SLAB_N) setmaxnreg_inc<Cfg::kRegsEpi>();
+    if constexpr (SLAB_N) {
+      // Two 256-column slabs fill TMEM, so the next tile's UMMAs wait until
+      // every epilogue warp has read both slabs out. Between the two reads only
+      // arithmetic happens: slab 0's C is prefetched into registers while the
+      // UMMAs run, slab 0 is blended and rounded in registers (its TMEM handed
+      // back first), slab 1 is read and handed back, and only then do results
+      // leave through the staging buffers. C is TMA-addressable here (16-byte
+      // aligned rows, N % 8 == 0; the launcher picks another tile otherwise).
+      static_assert(Cfg::kEpiChunks == 4 && Cfg::kEpiCols == 128, "slab-N epilogue layout");
+      const int ew = warp - Cfg::kEpiWarp0;
+      const int quad = warp & 3;     // TMEM lane quadrant accessible by this warp
+      const int col_half = ew >> 2;  // which 128-column half of each slab this warp owns
+      const bool read_c = p.beta != 0.0f;
+      const uint32_t buf0 = sEpi + static_cast<uint32_t>(ew * 2 * Cfg::kEpiBufBytes);
+      uint32_t tile_phase = 0;
+      bool ok = true;
+      // C of 128 columns of this thread's row, as packed halves (zero outside C).
+      auto load_c_row = [&](uint32_t (&cw)[64], int row, int col0) {
+        const half* crow = p.C + static_cast<size_t>(row < p.M ? row : 0) * p.ldc + col0;
+#pragma unroll
+        for (int g = 0; g < 16; ++g) {
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (row < p.M && col0 + 8 * g + 8 <= p.N) v = *reinterpret_cast<const uint4*>(crow + 8 * g);
+          cw[4 * g + 0] = v.x;
+          cw[4 * g + 1] = v.y;
+          cw[4 * g + 2] = v.z;
+          cw[4 * g + 3] = v.w;
+        }
+      };
+      // alpha * acc + beta * C for all 128 columns; results replace C in cw.
+      auto blend_row = [&](uint32_t (&cw)[64], const uint32_t (&a)[128]) {
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          const float c0 = read_c ? half_bits_to_float(cw[j] & 0xFFFFu) : 0.0f;
+          const float c1 = read_c ? half_bits_to_float(cw[j] >> 16) : 0.0f;
+          cw[j] = pack_half2(fmaf(p.alpha, __uint_as_float(a[2 * j]), p.beta * c0),
+                             fmaf(p.alpha, __uint_as_float(a[2 * j + 1]), p.beta * c1));
+        }
+      };
+      // Read one slab share from TMEM (128 columns of this warp's 32 lanes)
+      // and hand the slab back to the UMMA issuer.
+      auto drain_slab = [&](uint32_t (&a)[128], int sl) {
+        if (!mbar_wait_warp(tfull_bar(0, sl), tile_phase, p.timeout_ns, abort_flag, p.err,
+                            kErrTimeoutEpilogue))
+          return false;
+        tc_fence_after();
+        const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                static_cast<uint32_t>(sl * BN + col_half * Cfg::kEpiCols);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          tmem_ld_32x32b_x32(t_addr + i * 32, *reinterpret_cast<uint32_t(*)[32]>(&a[32 * i]));
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader)
+            mbar_arrive(tempty_bar(0, sl));
+          else
+            mbar_arrive_remote_signal(mapa_shared(tempty_bar(0, sl), 0));
+        }
+        return true;
+      };
+      // Results of 128 columns out through the two staging buffers (32 x 32
+      // boxes, 64B-swizzled rows, lane = row), TMA-stored.
+      auto store_row = [&](const uint32_t (&cw)[64], int row_base, int col0) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t buf = buf0 + (c & 1) * Cfg::kEpiBufBytes;
+          if (lane == 0) bulk_wait_read<1>();  // the store two boxes back has read this buffer
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t addr = buf + static_cast<uint32_t>(lane) * 64u +
+                                  static_cast<uint32_t>((q ^ ((lane >> 1) & 3)) * 16);
+            st_shared_v4(addr, make_uint4(cw[16 * c + 4 * q], cw[16 * c + 4 * q + 1],
+                                          cw[16 * c + 4 * q + 2], cw[16 * c + 4 * q + 3]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            // a box that starts past the last row or column writes nothing: skip it
+            if (row_base < p.M && col0 + 32 * c < p.N)
+              tma_store_2d(&tmap_c, buf, col0 + 32 * c, row_base);
+            bulk_commit_group();
+          }
+        }
+      };
+      for (int t = unit; t < num_tiles && ok; t += num_units) {
+        int tm, tn;
+        tile_coords(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
+        const int row_base = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kCtaRows + quad * 32;
+        const int col0_s0 = tn * Cfg::kTileN + col_half * Cfg::kEpiCols;
+        const int col0_s1 = col0_s0 + BN;
+        uint32_t cw[64];
+        uint32_t a[128];
+        if (read_c) load_c_row(cw, row_base + lane, col0_s0);
+        if (!drain_slab(a, 0)) {
+          ok = false;
+          break;
+        }
+        blend_row(cw, a);
+        if (!drain_slab(a, 1)) {  // after this the next tile's UMMAs may start
+          ok = false;
+          break;
+        }
+        store_row(cw, row_base, col0_s0);
+        if (read_c) load_c_row(cw, row_base + lane, col0_s1);
+        blend_row(cw, a);
+        store_row(cw, row_base, col0_s1);
+        tile_phase ^= 1u;
+      }
+      if (lane == 0) bulk_wait_all();  // every TMA store of this warp has landed
+    } else {
+      const int ew = warp - Cfg::kEpiWarp0;
+      const int quad = warp & 3;      // TMEM lane quadrant accessible by this warp
+      const int col_half = ew >> 2;   // which half of the tile's columns this warp owns
+      const bool read_c = p.beta != 0.0f;
+      const uint32_t buf0 = sEpi + static_cast<uint32_t>(ew * 2 * Cfg::kEpiBufBytes);
+      float* lsu_tile = epi_float + ew * 32 * 33;
+      // Staging buffer of chunk i (counted over the whole kernel) is i & 1; with
+      // beta != 0 each buffer's C-load barrier completes once per use.
+      uint32_t ctr = 0;
+      uint32_t cwait[2] = {0u, 0u};
+      auto issue_c_load = [&](uint32_t chunk_index, int col, int row) {
+        const uint32_t b = chunk_index & 1u;
+        mbar_arrive_expect_tx(cload_bar(ew, b), Cfg::kEpiBufBytes);
+        tma_load_2d<false>(buf0 + b * Cfg::kEpiBufBytes, &tmap_c, cload_bar(ew, b), col, row);
+      };
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+      constexpr int kChunks = Cfg::kEpiChunks;
       for (int t = unit; t < num_tiles && ok; t += num_units) {
-        for (int kb = 0; kb < p.num_kb && ok; ++kb) {
-          if (!mbar_wait_warp(full_bar(stage), phase, p.timeout_ns, abort_flag, p.err,
-                              kErrTimeoutMma)) {
+        int tm, tn;
+        tile_coords(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
+        for (int sl = 0; sl < SLABS && ok; ++sl) {
+          const int row_base = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kCtaRows +
+                               sl * Cfg::BM + quad * 32;
+          const int col_base = tn * Cfg::kTileN + col_half * Cfg::kEpiCols;
+          // Prefetch this slab's first two C boxes while its UMMAs still run.
+          if (p.c_tma && read_c && lane == 0) {
+            bulk_wait_read<0>();  // earlier TMA stores have finished reading both buffers
+            issue_c_load(ctr, col_base, row_base);
+            if (kChunks > 1) issue_c_load(ctr + 1, col_base + Cfg::kEpiChunk, row_base);
+          }
+          if (!mbar_wait_warp(tfull_bar(acc, sl), acc_phase, p.timeout_ns, abort_flag, p.err,
+                              kErrTimeoutEpilogue)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = sA0 + stage * Cfg::kABytes;
-          const uint32_t b_addr = sB0 + stage * Cfg::kBBytes;
-          if constexpr (SLAB_N) {
-            // Both N slabs take the same A: fill the A collector on slab 0 and
-            // reuse it on slab 1. Both accumulators must be free before kb 0.
-            if (kb == 0) {
-#pragma unroll
-              for (int sl = 0; sl < SLABS; ++sl)
-                if (ok && !mbar_wait_warp(tempty_bar(acc, sl), acc_phase ^ 1u, p.timeout_ns,
-                                          abort_flag, p.err, kErrTimeoutMma))
-                  ok = false;
-              if (!ok) break;
-              tc_fence_after();
-            }
-#pragma unroll
-            for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
-              const uint64_t adesc = make_smem_desc(a_addr + kk * 32, 16, 1024);
-              const uint32_t en = (kb | kk) != 0 ? 1u : 0u;
-              const uint32_t d0 = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
-              const uint64_t b0 = BKM ? make_smem_desc(b_addr + kk * 32, 16, 1024)
-                                      : make_smem_desc(b_addr + kk * 2048, Cfg::kBBoxBytes, 1024);
-              const uint64_t b1 =
-                  BKM ? make_smem_desc(b_addr + Cfg::kBSlabBytes + kk * 32, 16, 1024)
-                      : make_smem_desc(b_addr + Cfg::kBSlabBytes + kk * 2048, Cfg::kBBoxBytes,
-                                       1024);
-              if (elect_one()) {
-                umma_f16<PAIR, 1>(d0, adesc, b0, idesc, en);
-                umma_f16<PAIR, 2>(d0 + BN, adesc, b1, idesc, en);
-              }
-              __syncwarp();
-            }
-            if (kb == p.num_kb - 1) {
-              if (elect_one()) {
-#pragma unroll
-                for (int sl = 0; sl < SLABS; ++sl) umma_commit_to<PAIR>(tfull_bar(acc, sl));
-              }
-              __syncwarp();
-            }
-          } else {
-#pragma unroll
-            for (int sl = 0; sl < SLABS; ++sl) {
-              if (kb == 0) {
-                // this slab's accumulator must have been drained by the epilogue
-                if (!mbar_wait_warp(tempty_bar(acc, sl), acc_phase ^ 1u, p.timeout_ns, abort_flag,
-                                    p.err, kErrTimeoutMma)) {
+          // Whole share of the slab into registers, then hand TMEM back at once.
+          uint32_t r[Cfg::kEpiCols];
+          const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                  static_cast<uint32_t>(acc * Cfg::kAccCols + sl * BN +
+                                                        col_half * Cfg::kEpiCols);
+  #pragma unroll
+          for (int i = 0; i < kChunks; ++i)
+            tmem_ld_32x32b_x32(t_addr + i * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * i]));
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            // the even CTA's barrier gates the next tile's UMMAs
+            if (PAIR && !leader)
+              mbar_arrive_remote_signal(mapa_shared(tempty_bar(acc, sl), 0));
+            else
+              mbar_arrive(tempty_bar(acc, sl));
+          }
+  #pragma unroll
+          for (int c = 0; c < kChunks; ++c) {
+            const int col0 = col_base + c * Cfg::kEpiChunk;
+            if (p.c_tma) {
+              const uint32_t b = ctr & 1u;
+              const uint32_t buf = buf0 + b * Cfg::kEpiBufBytes;
+              if (read_c) {
+                if (!mbar_wait_warp(cload_bar(ew, b), cwait[b] & 1u, p.timeout_ns, abort_flag,
+                                    p.err, kErrTimeoutEpilogue)) {
                   ok = false;
                   break;
                 }
-                tc_fence_after();
+                ++cwait[b];
+              } else if (lane == 0) {
+                bulk_wait_read<1>();  // this buffer's previous store has read it
               }
-              const uint32_t d_tmem =
-                  tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols + sl * BN);
-#pragma unroll
-              for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
-                // A: K-major, 128B swizzle; advance 16 K-elements = 32 bytes
-                // inside the swizzle row. SBO = 8 rows * 128 B.
-                const uint64_t adesc =
-                    make_smem_desc(a_addr + sl * Cfg::kSlabBytes + kk * 32, 16, 1024);
-                // B, N-major: 128B swizzle; 16 K-rows = two 8-row groups of
-                // 1024 B. LBO = distance between 64-column boxes, SBO = 8 K-rows.
-                // B, K-major: laid out like A (rows of 64 K, 32 bytes per K step).
-                const uint64_t bdesc =
-                    BKM ? make_smem_desc(b_addr + kk * 32, 16, 1024)
-                        : make_smem_desc(b_addr + kk * 2048, Cfg::kBBoxBytes, 1024);
-                if (elect_one())
-                  umma_f16<PAIR>(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
-                __syncwarp();
+              __syncwarp();
+              // lane = row: four 16-byte pieces of 8 columns, 64B-swizzled rows
+              const uint32_t row_addr = buf + static_cast<uint32_t>(lane) * 64u;
+  #pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const uint32_t addr =
+                    row_addr + static_cast<uint32_t>(((q ^ ((lane >> 1) & 3)) * 16));
+                uint4 cv = make_uint4(0, 0, 0, 0);
+                if (read_c) cv = ld_shared_v4(addr);
+                const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
+                uint32_t o[4];
+  #pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  const float c0 = read_c ? half_bits_to_float(cw[h] & 0xFFFFu) : 0.0f;
+                  const float c1 = read_c ? half_bits_to_float(cw[h] >> 16) : 0.0f;
+                  o[h] = pack_half2(
+                      fmaf(p.alpha, __uint_as_float(r[32 * c + 8 * q + 2 * h]), p.beta * c0),
+                      fmaf(p.alpha, __uint_as_float(r[32 * c + 8 * q + 2 * h + 1]), p.beta * c1));
+                }
+                st_shared_v4(addr, make_uint4(o[0], o[1], o[2], o[3]));
               }
-              if (kb == p.num_kb - 1) {
-                if (elect_one()) umma_commit_to<PAIR>(tfull_bar(acc, sl));
-                __syncwarp();
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                // a box that starts past the last row or column writes nothing: skip it
+                if (row_base < p.M && col0 < p.N) {
+                  tma_store_2d(&tmap_c, buf, col0, row_base);
+                  bulk_commit_group();
+                }
+                if (read_c && c + 2 < kChunks) {
+                  bulk_wait_read<0>();  // the store just issued has read this buffer
+                  issue_c_load(ctr + 2, col0 + 2 * Cfg::kEpiChunk, row_base);
+                }
               }
+            } else {
+              epilogue_chunk_lsu(p, lsu_tile, row_base, col0, &r[32 * c], lane);
             }
-          }
-          if (!ok) break;
-          if (elect_one()) umma_commit_to<PAIR>(empty_bar(stage));
-          __syncwarp();
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
+            ++ctr;
           }
         }
         if (++acc == Cfg::kAccBufs) {
@@ -454,133 +719,8 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
           acc_phase ^= 1u;
         }
       }
-      // Drain: all UMMAs issued by the elected lane complete before TMEM is freed.
-      if (elect_one()) umma_commit_local<PAIR>(final_bar);
-      __syncwarp();
-      volatile int no_abort = 0;
-      mbar_wait_warp(final_bar, 0, p.timeout_ns, &no_abort, p.err, kErrTimeoutMma);
+      if (lane == 0) bulk_wait_all();  // every TMA store of this warp has landed
     }
-  } else {
-    // ---------------- Epilogue (warps 2..9 of every CTA) ----------------
-    const int ew = warp - 2;
-    const int quad = warp & 3;      // TMEM lane quadrant accessible by this warp
-    const int col_half = ew >> 2;   // which half of the tile's columns this warp owns
-    const bool read_c = p.beta != 0.0f;
-    const uint32_t buf0 = sEpi + static_cast<uint32_t>(ew * 2 * Cfg::kEpiBufBytes);
-    float* lsu_tile = epi_float + ew * 32 * 33;
-    // Staging buffer of chunk i (counted over the whole kernel) is i & 1; with
-    // beta != 0 each buffer's C-load barrier completes once per use.
-    uint32_t ctr = 0;
-    uint32_t cwait[2] = {0u, 0u};
-    auto issue_c_load = [&](uint32_t chunk_index, int col, int row) {
-      const uint32_t b = chunk_index & 1u;
-      mbar_arrive_expect_tx(cload_bar(ew, b), Cfg::kEpiBufBytes);
-      tma_load_2d<false>(buf0 + b * Cfg::kEpiBufBytes, &tmap_c, cload_bar(ew, b), col, row);
-    };
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    bool ok = true;
-    constexpr int kChunks = Cfg::kEpiChunks;
-    for (int t = unit; t < num_tiles && ok; t += num_units) {
-      int tm, tn;
-      tile_coords(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
-      for (int sl = 0; sl < SLABS && ok; ++sl) {
-        const int row_base = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kCtaRows +
-                             (SLAB_N ? 0 : sl * Cfg::BM) + quad * 32;
-        const int col_base =
-            tn * Cfg::kTileN + (SLAB_N ? sl * BN : 0) + col_half * Cfg::kEpiCols;
-        // Prefetch this slab's first two C boxes while its UMMAs still run.
-        if (p.c_tma && read_c && lane == 0) {
-          bulk_wait_read<0>();  // earlier TMA stores have finished reading both buffers
-          issue_c_load(ctr, col_base, row_base);
-          if (kChunks > 1) issue_c_load(ctr + 1, col_base + Cfg::kEpiChunk, row_base);
-        }
-        if (!mbar_wait_warp(tfull_bar(acc, sl), acc_phase, p.timeout_ns, abort_flag, p.err,
-                            kErrTimeoutEpilogue)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // Whole share of the slab into registers, then hand TMEM back at once.
-        uint32_t r[Cfg::kEpiCols];
-        const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                                static_cast<uint32_t>(acc * Cfg::kAccCols + sl * BN +
-                                                      col_half * Cfg::kEpiCols);
-#pragma unroll
-        for (int i = 0; i < kChunks; ++i)
-          tmem_ld_32x32b_x32(t_addr + i * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * i]));
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          // the even CTA's barrier gates the next tile's UMMAs
-          if (PAIR && !leader)
-            mbar_arrive_remote_signal(mapa_shared(tempty_bar(acc, sl), 0));
-          else
-            mbar_arrive(tempty_bar(acc, sl));
-        }
-#pragma unroll
-        for (int c = 0; c < kChunks; ++c) {
-          const int col0 = col_base + c * Cfg::kEpiChunk;
-          if (p.c_tma) {
-            const uint32_t b = ctr & 1u;
-            const uint32_t buf = buf0 + b * Cfg::kEpiBufBytes;
-            if (read_c) {
-              if (!mbar_wait_warp(cload_bar(ew, b), cwait[b] & 1u, p.timeout_ns, abort_flag,
-                                  p.err, kErrTimeoutEpilogue)) {
-                ok = false;
-                break;
-              }
-              ++cwait[b];
-            } else if (lane == 0) {
-              bulk_wait_read<1>();  // this buffer's previous store has read it
-            }
-            __syncwarp();
-            // lane = row: four 16-byte pieces of 8 columns, 64B-swizzled rows
-            const uint32_t row_addr = buf + static_cast<uint32_t>(lane) * 64u;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint32_t addr =
-                  row_addr + static_cast<uint32_t>(((q ^ ((lane >> 1) & 3)) * 16));
-              uint4 cv = make_uint4(0, 0, 0, 0);
-              if (read_c) cv = ld_shared_v4(addr);
-              const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
-              uint32_t o[4];
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                const float c0 = read_c ? half_bits_to_float(cw[h] & 0xFFFFu) : 0.0f;
-                const float c1 = read_c ? half_bits_to_float(cw[h] >> 16) : 0.0f;
-                o[h] = pack_half2(
-                    fmaf(p.alpha, __uint_as_float(r[32 * c + 8 * q + 2 * h]), p.beta * c0),
-                    fmaf(p.alpha, __uint_as_float(r[32 * c + 8 * q + 2 * h + 1]), p.beta * c1));
-              }
-              st_shared_v4(addr, make_uint4(o[0], o[1], o[2], o[3]));
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              // a box that starts past the last row or column writes nothing: skip it
-              if (row_base < p.M && col0 < p.N) {
-                tma_store_2d(&tmap_c, buf, col0, row_base);
-                bulk_commit_group();
-              }
-              if (read_c && c + 2 < kChunks) {
-                bulk_wait_read<0>();  // the store just issued has read this buffer
-                issue_c_load(ctr + 2, col0 + 2 * Cfg::kEpiChunk, row_base);
-              }
-            }
-          } else {
-            epilogue_chunk_lsu(p, lsu_tile, row_base, col0, &r[32 * c], lane);
-          }
-          ++ctr;
-        }
-      }
-      if (++acc == Cfg::kAccBufs) {
-        acc = 0;
-        acc_phase ^= 1u;
-      }
-    }
-    if (lane == 0) bulk_wait_all();  // every TMA store of this warp has landed
   }
 
   tc_fence_before();
