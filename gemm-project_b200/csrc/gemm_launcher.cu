@@ -981,6 +981,23 @@ extern "C" GEMM_API int gemm_launcher_status(void) {
   return status;
 }
 
+extern "C" GEMM_API int gemm_launch_error(void) {
+  const int status = tl_status;
+  tl_status = 0;
+  return status;
+}
+
+extern "C" GEMM_API bool launchGemmSample(const half* a, const half* b, half* c, int m, int n,
+                                          int k, cudaStream_t stream) {
+  // The reference sample's acceptance rule (samples/trtllm_gemm/launcher.cu:6-11).
+  const auto addresses = reinterpret_cast<std::uintptr_t>(a) | reinterpret_cast<std::uintptr_t>(b) |
+                         reinterpret_cast<std::uintptr_t>(c);
+  if (m < 1 || m > 16 || n < 512 || n % 64 != 0 || k < 512 || k % 32 != 0 || (addresses & 15u))
+    return false;
+  dispatch(a, b, c, m, n, k, 1.0f, 0.0f, stream, 0, 0);
+  return true;
+}
+
 extern "C" GEMM_API const char* gemm_last_kernel(void) { return tl_last_kernel; }
 
 extern "C" GEMM_API int gemm_slab_rows(int M, int world, int rank, int* row0) {

@@ -50,6 +50,10 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gemm_launcher_noalloc.restype = i
     lib.gemm_launcher_tn.argtypes = gemm8 + [vp, i]
     lib.gemm_launcher_tn.restype = i
+    lib.launchGemmSample.argtypes = [vp, vp, vp, i, i, i, vp]
+    lib.launchGemmSample.restype = ctypes.c_bool
+    lib.gemm_launch_error.argtypes = []
+    lib.gemm_launch_error.restype = i
     return lib
 
 
@@ -65,6 +69,27 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     if path is None:
         _lib = lib
     return lib
+
+
+TORCH_OP_PATH = PKG_ROOT / "lib" / "libgemm_torch_op.so"
+_torch_ops_loaded = False
+
+
+def load_torch_ops(path: str | os.PathLike | None = None):
+    """Register the PyTorch operators (torch.ops.trtllm_gemm_sample.gemm,
+    torch.ops.gemm_b200.gemm, torch.ops.gemm_b200.linear) from
+    libgemm_torch_op.so and return torch.ops. Raises GemmError if the library
+    is absent (build it with `python gemm-project_b200/build.py --torch-op`)."""
+    global _torch_ops_loaded
+    import torch
+    p = Path(path) if path is not None else TORCH_OP_PATH
+    if not _torch_ops_loaded:
+        if not p.exists():
+            raise GemmError(f"{p} is missing: build it with "
+                            "`python gemm-project_b200/build.py --torch-op`")
+        torch.ops.load_library(str(p))
+        _torch_ops_loaded = True
+    return torch.ops
 
 
 def _stream_handle(stream) -> int:

@@ -12,6 +12,10 @@
 
 #include <cuda_runtime_api.h>
 
+#ifndef __cplusplus
+#include <stdbool.h>
+#endif
+
 #ifdef __cplusplus
 #include <cuda_fp16.h>
 typedef __half gemm_half_t;
@@ -71,6 +75,27 @@ GEMM_API int gemm_launcher_ex(const gemm_half_t* A, const gemm_half_t* B, gemm_h
 GEMM_API int gemm_launcher_tn(const gemm_half_t* A, const gemm_half_t* Bt, gemm_half_t* C, int M,
                               int N, int K, float alpha, float beta, cudaStream_t stream,
                               int tile_n);
+
+/* Drop-in for the reference's stream-aware inference launcher,
+ * samples/trtllm_gemm/launcher.cu:4-23 (`extern "C" bool launchGemmSample(half
+ * const* a, half const* b, half* c, int m, int n, int k, cudaStream_t
+ * stream)`), which its PyTorch binding samples/trtllm_gemm/binding.cpp:12-13
+ * declares and calls. Same acceptance rule and return value: false, with
+ * nothing launched, unless 1 <= m <= 16, n >= 512, n % 64 == 0, k >= 512,
+ * k % 32 == 0 and a, b, c are 16-byte aligned; otherwise C = A * B (alpha 1,
+ * beta 0) is launched on `stream` through the same dispatch as
+ * gemm_launcher_stream and true is returned. Launch errors are reported by
+ * gemm_launch_error(), not by the return value. */
+GEMM_API bool launchGemmSample(const gemm_half_t* a, const gemm_half_t* b, gemm_half_t* c, int m,
+                               int n, int k, cudaStream_t stream);
+
+/* The first launch error recorded on this thread since the last call (a
+ * cudaError_t value, 0 if none), cleared by the call. Unlike
+ * gemm_launcher_status() it reads no device memory and never synchronizes, so
+ * operator bindings call it after every launch, also inside CUDA graph
+ * capture. (This library links the CUDA runtime statically: the caller's own
+ * cudaGetLastError() does not see its launches.) */
+GEMM_API int gemm_launch_error(void);
 
 /* gemm_launcher_stream for callers that cannot let a library allocate device
  * memory. No counterpart in the reference.
