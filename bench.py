@@ -53,59 +53,77 @@ def peaks():
 
 
 # ---------------------------------------------------------------------------
-# clocks sampler (nvidia-smi during the timed region)
+# clocks sampler (NVML, every few ms, during the timed region)
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock, power and clock-event (throttle) reasons of one GPU, polled
+    through NVML (the data nvidia-smi's clocks line reads) every `period_s`
+    from a thread while the timed region runs: timed regions of tens of
+    milliseconds still get samples. Reading only; no GPU setting is touched."""
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines: list[str] = []
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+
+    def __init__(self, device, period_s: float = 0.005):
+        self.device = device
+        self.period = period_s
+        self.sm: list[float] = []
+        self.power: list[float] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._handle = None
+
+    def _open(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:  # match the CUDA device to its NVML handle by PCI address
+            props = torch.cuda.get_device_properties(self.device)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(torch.device(self.device).index or 0)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except FileNotFoundError:
-            self.proc = None
+            self.nvml, self._handle = self._open()
+            self.max_mhz = float(self.nvml.nvmlDeviceGetMaxClockInfo(self._handle,
+                                                                     self.nvml.NVML_CLOCK_SM))
+        except Exception:
+            self._handle = None
+            return self
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nv, h = self.nvml, self._handle
+        while not self._stop.is_set():
+            try:
+                self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                self.power.append(nv.nvmlDeviceGetPowerUsage(h) / 1000.0)
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for name, const in self.REASONS:
+                    if mask & getattr(nv, const, 0):
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(self.period)
 
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        if self._handle is not None:
+            self.thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(self.sm) if self.sm else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.sm),
+                "power_w": round(statistics.median(self.power), 1) if self.power else None,
+                "source": "NVML, sampled every 5 ms during the timed region"}
 
 
 # ---------------------------------------------------------------------------
@@ -138,11 +156,55 @@ def offset_copy(t, off):
     return v
 
 
-def time_calls(fn, steps, warmup, stream):
-    """Average ms per call over `steps` back-to-back calls (CUDA events on `stream`)."""
-    for _ in range(warmup):
+def warm_up(fn, calls, seconds):
+    """At least `calls` untimed calls and at least `seconds` of wall time of
+    calls, so that the GPU has reached its steady, power-capped clock before a
+    timed region starts (right after idle it runs faster for a while, and a
+    short timed region would catch that transient). Returns the calls made."""
+    n = 0
+    for _ in range(calls):
         fn()
+        n += 1
     torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        for _ in range(8):
+            fn()
+            n += 1
+        torch.cuda.synchronize()
+    return n
+
+
+def time_block(fn, steps, stream):
+    """ms per call over `steps` back-to-back calls, CUDA events on `stream`."""
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps
+
+
+def paired_ms(fn_ours, fn_ref, steps, warmup, stream, rounds=5, warm_s=0.5):
+    """Median ms per call of two implementations timed in alternating blocks
+    (ours, ref, ours, ref, ...) after both are warm, so that both see the same
+    power-capped clock (on a 1 kW B200 it drifts with temperature)."""
+    warm_up(fn_ours, warmup, warm_s)
+    warm_up(fn_ref, warmup, warm_s / 4)
+    t_ours, t_ref = [], []
+    for _ in range(rounds):
+        t_ours.append(time_block(fn_ours, steps, stream))
+        t_ref.append(time_block(fn_ref, steps, stream))
+    return statistics.median(t_ours), statistics.median(t_ref)
+
+
+def time_calls(fn, steps, warmup, stream, warm_s=0.5):
+    """Average ms per call over `steps` back-to-back calls (CUDA events on
+    `stream`), after warm_up(fn, warmup, warm_s)."""
+    warm_up(fn, warmup, warm_s)
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record(stream)
@@ -214,9 +276,10 @@ def measure_config(gb, name, cfg, stream, steps, warmup, device, tn=False):
     alpha, beta = cfg["alpha"], cfg["beta"]
     c_ours = c.clone() if off == 0 else offset_copy(c, off)
     c_cub = c.clone()
-    ms = time_calls(lambda: gb.gemm(a, b, c_ours, alpha, beta, stream), steps, warmup, stream)
+    ms, ms_cub = paired_ms(lambda: gb.gemm(a, b, c_ours, alpha, beta, stream),
+                           lambda: gb.cublas(a, b, c_cub, alpha, beta, stream), steps, warmup, stream)
+    gb.gemm(a, b, c_ours, alpha, beta, stream)
     kernel = gb.last_kernel()
-    ms_cub = time_calls(lambda: gb.cublas(a, b, c_cub, alpha, beta, stream), steps, warmup, stream)
     flops = 2.0 * m * n * k
     bytes_ = 2.0 * (m * k + k * n + m * n) + (2.0 * m * n if beta != 0 else 0.0)
     return {"M": m, "N": n, "K": k, "kernel": kernel, "us": ms * 1e3, "cublas_us": ms_cub * 1e3,
@@ -232,12 +295,10 @@ def run_single(args, gb, oracle_cfgs, device, pk):
     a, b, c = dev_inputs(m, n, k, "normal", "uniform", 0, device)
     flops = 2.0 * m * n * k
     steps, warmup = args.steps, max(args.warmup, 3)
-    # warm-up (untimed)
-    for _ in range(warmup):
-        gb.gemm(a, b, c, alpha, beta, stream)
-    torch.cuda.synchronize()
+    # warm-up (untimed): at least `warmup` steps and one second, to steady clocks
+    warm_run = warm_up(lambda: gb.gemm(a, b, c, alpha, beta, stream), warmup, 1.0)
     kernel = gb.last_kernel()
-    with ClockSampler(device.index) as clk:
+    with ClockSampler(device) as clk:
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
@@ -272,7 +333,10 @@ def run_single(args, gb, oracle_cfgs, device, pk):
     h2d = (a.numel() + b.numel() + c.numel()) * 2
     d2h = c.numel() * 2
 
-    ms_cub = time_calls(lambda: gb.cublas(a, b, c, alpha, beta, stream), steps, warmup, stream)
+    # cuBLAS on the same inputs, in blocks alternating with ours (the ratio's basis)
+    ms_pair, ms_cub = paired_ms(lambda: gb.gemm(a, b, c, alpha, beta, stream),
+                                lambda: gb.cublas(a, b, c, alpha, beta, stream), steps, warmup,
+                                stream)
 
     # other single-GPU configs (each next to cuBLAS on the same inputs)
     configs = {}
@@ -299,7 +363,8 @@ def run_single(args, gb, oracle_cfgs, device, pk):
                                                           budget_s=args.cpu_budget)
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": 1,
-        "steps": steps, "warmup": warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "steps": steps, "warmup": warmup, "warmup_steps_run": warm_run,
+        "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp16 in, fp32 accumulate",
         "data": "synthetic (seeded on device: A,B ~ N(0,1/sqrt(K)), C ~ U[-1,1))",
         "config": {"workload": "square FP16 GEMM M=N=K=8192, alpha=1, beta=0.5 (BASELINE configs[1])",
@@ -307,7 +372,9 @@ def run_single(args, gb, oracle_cfgs, device, pk):
                    "l2": "inputs (384 MiB) larger than the 126 MB L2; no flush"},
         "roofline": roof,
         "cublas": {"tflops": round(flops / ms_cub / 1e9, 2), "ms": round(ms_cub, 4),
-                   "ours_vs_cublas": round(ms_cub / ms, 4)},
+                   "ours_tflops_paired": round(flops / ms_pair / 1e9, 2),
+                   "ours_vs_cublas": round(ms_cub / ms_pair, 4),
+                   "method": "median of 5 alternating blocks of `steps` calls each, both warm"},
         "e2e": {"value": round(flops / e2e_ms / 1e9, 3), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "api": "gemm_launcher_stream via ctypes, pinned host buffers"},
@@ -363,11 +430,10 @@ def run_multi(args, gb, oracle_cfgs, device, pk, rank, world):
     a = (torch.randn((slab_m, k), generator=g, device=device) / math.sqrt(k)).half()
     c = torch.zeros((slab_m, n), device=device, dtype=torch.float16)
     warmup = max(args.warmup, 3)
-    for _ in range(warmup):
-        gb.gemm(a, b, c, alpha, beta, stream)
-    torch.cuda.synchronize()
+    # at least `warmup` steps and one second per rank (no collective inside)
+    warm_run = warm_up(lambda: gb.gemm(a, b, c, alpha, beta, stream), warmup, 1.0)
     dist.barrier()
-    with ClockSampler(device.index) as clk:
+    with ClockSampler(device) as clk:
         torch.cuda.synchronize()
         dist.barrier()
         start = torch.cuda.Event(enable_timing=True)
@@ -408,7 +474,8 @@ def run_multi(args, gb, oracle_cfgs, device, pk, rank, world):
         return None
     return {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": warmup, "ms_per_step": round(ms_v, 4),
+        "steps": args.steps, "warmup": warmup, "warmup_steps_run": warm_run,
+        "ms_per_step": round(ms_v, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "fp16 in, fp32 accumulate",
         "data": "synthetic (seeded on device: A,B ~ N(0,1/sqrt(K)), C = 0)",
