@@ -349,7 +349,8 @@ int raster_group(int tiles_m, int tiles_n) {
 
 template <int BN, bool PAIR, bool BKM, int SLABS, bool SLAB_N = false>
 void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
-                  const TcParams& p, const DeviceInfo& d, cudaStream_t s, int M, int N, int K) {
+                  const TcParams& p, const DeviceInfo& d, cudaStream_t s, int M, int N, int K,
+                  int max_sms) {
   using Cfg = TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>;
   const int tiles = p.tiles_m * p.tiles_n;
   static const char* names[2][6] = {
@@ -364,7 +365,8 @@ void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   const char* name = names[BKM ? 1 : 0][idx];
   if constexpr (PAIR) {
     const int cap = SLAB_N ? d.pairn_clusters : (SLABS == 2 ? d.pair2_clusters : d.pair_clusters);
-    const int clusters = std::min(tiles, cap);
+    const int clusters =
+        std::min(tiles, max_sms > 0 ? std::min(cap, std::max(1, max_sms / 2)) : cap);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
@@ -381,7 +383,7 @@ void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     record_error(
         cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, true, BKM, SLABS, SLAB_N>, ta, tb, tc, p));
   } else {
-    const int grid = std::min(tiles, d.sms);
+    const int grid = std::min(tiles, max_sms > 0 ? std::min(d.sms, max_sms) : d.sms);
     log_launch(name, M, N, K, dim3(grid), dim3(Cfg::kThreads));
     tc_gemm_kernel<BN, false, BKM, SLABS, SLAB_N>
         <<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(ta, tb, tc, p);
@@ -394,7 +396,8 @@ void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
 // b_kmajor: B is given as Bt[N,K] (row pitch ldb), i.e. C = A * Bt^T.
 int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half* C, int M, int N,
                    int K, float alpha, float beta, cudaStream_t s, int tile, const DeviceInfo& d,
-                   bool b_kmajor = false) {
+                   bool b_kmajor = false, int ldc = 0, int max_sms = 0) {
+  if (ldc <= 0) ldc = N;
   const bool pair = tile == kTilePair || tile == kTilePair2 || tile == kTilePairN;
   const int slabs = tile == kTilePair2 ? 2 : 1;  // A slabs per CTA
   CUtensorMap ta, tb, tc;
@@ -406,8 +409,8 @@ int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half*
   const bool ok_a =
       make_tmap(&ta, a_src, K, M, static_cast<uint64_t>(lda) * 2, 64, 128u * slabs);
   // C goes through TMA (32 x 32 boxes, 64B swizzle) when it is TMA-addressable.
-  const int c_tma = aligned16(C) && N % 8 == 0 &&
-                    make_tmap(&tc, C, N, M, static_cast<uint64_t>(N) * 2, 32, 32,
+  const int c_tma = aligned16(C) && ldc % 8 == 0 &&
+                    make_tmap(&tc, C, N, M, static_cast<uint64_t>(ldc) * 2, 32, 32,
                               CU_TENSOR_MAP_SWIZZLE_64B);
   if (!(ok_a && ok_b)) {
     record_error(cudaErrorInvalidValue);
@@ -422,7 +425,7 @@ int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half*
   p.M = M;
   p.N = N;
   p.K = K;
-  p.ldc = N;
+  p.ldc = ldc;
   p.alpha = alpha;
   p.beta = beta;
   p.tiles_m = ceil_div(M, tile_m);
@@ -430,26 +433,26 @@ int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half*
   p.num_kb = ceil_div(K, 64);
   p.group = raster_group(p.tiles_m, p.tiles_n);
   p.c_tma = c_tma;
-  p.c_vec_ok = aligned16(C) && N % 8 == 0;
+  p.c_vec_ok = aligned16(C) && ldc % 8 == 0;
   p.timeout_ns = wait_timeout_ns();
   p.err = d.err;
   if (b_kmajor) {
     switch (tile) {
-      case 64: launch_tc_bn<64, false, true, 1>(ta, tb, tc, p, d, s, M, N, K); break;
-      case 128: launch_tc_bn<128, false, true, 1>(ta, tb, tc, p, d, s, M, N, K); break;
-      case kTilePair: launch_tc_bn<256, true, true, 1>(ta, tb, tc, p, d, s, M, N, K); break;
-      case kTilePair2: launch_tc_bn<256, true, true, 2>(ta, tb, tc, p, d, s, M, N, K); break;
-      case kTilePairN: launch_tc_bn<256, true, true, 2, true>(ta, tb, tc, p, d, s, M, N, K); break;
-      default: launch_tc_bn<256, false, true, 1>(ta, tb, tc, p, d, s, M, N, K); break;
+      case 64: launch_tc_bn<64, false, true, 1>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+      case 128: launch_tc_bn<128, false, true, 1>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+      case kTilePair: launch_tc_bn<256, true, true, 1>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+      case kTilePair2: launch_tc_bn<256, true, true, 2>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+      case kTilePairN: launch_tc_bn<256, true, true, 2, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+      default: launch_tc_bn<256, false, true, 1>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
     }
   } else {
     switch (tile) {
-      case 64: launch_tc_bn<64, false, false, 1>(ta, tb, tc, p, d, s, M, N, K); break;
-      case 128: launch_tc_bn<128, false, false, 1>(ta, tb, tc, p, d, s, M, N, K); break;
-      case kTilePair: launch_tc_bn<256, true, false, 1>(ta, tb, tc, p, d, s, M, N, K); break;
-      case kTilePair2: launch_tc_bn<256, true, false, 2>(ta, tb, tc, p, d, s, M, N, K); break;
-      case kTilePairN: launch_tc_bn<256, true, false, 2, true>(ta, tb, tc, p, d, s, M, N, K); break;
-      default: launch_tc_bn<256, false, false, 1>(ta, tb, tc, p, d, s, M, N, K); break;
+      case 64: launch_tc_bn<64, false, false, 1>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+      case 128: launch_tc_bn<128, false, false, 1>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+      case kTilePair: launch_tc_bn<256, true, false, 1>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+      case kTilePair2: launch_tc_bn<256, true, false, 2>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+      case kTilePairN: launch_tc_bn<256, true, false, 2, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+      default: launch_tc_bn<256, false, false, 1>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
     }
   }
   return 0;
@@ -979,6 +982,18 @@ extern "C" GEMM_API int gemm_launcher_status(void) {
     if (status == 0) status = 1000 + dev_err;
   }
   return status;
+}
+
+extern "C" GEMM_API int gemm_launcher_sub(const half* A, int lda, const half* B, int ldb, half* C,
+                                          int ldc, int M, int N, int K, float alpha, float beta,
+                                          cudaStream_t stream, int max_sms) {
+  if (M <= 0 || N <= 0) return 0;
+  if (K <= 0 || lda < K || ldb < N || ldc < N || max_sms < 0) return -1;
+  // The tcgen05 kernels read A and B through TMA: 16-byte aligned bases and pitches.
+  if (!aligned16(A) || !aligned16(B) || lda % 8 != 0 || ldb % 8 != 0) return -1;
+  DeviceInfo& d = device_info();
+  return launch_tc_core(A, lda, B, ldb, C, M, N, K, alpha, beta, stream, choose_tile(M, N, d), d,
+                        /*b_kmajor=*/false, ldc, max_sms);
 }
 
 extern "C" GEMM_API int gemm_launch_error(void) {

@@ -54,6 +54,8 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.launchGemmSample.restype = ctypes.c_bool
     lib.gemm_launch_error.argtypes = []
     lib.gemm_launch_error.restype = i
+    lib.gemm_launcher_sub.argtypes = [vp, i, vp, i, vp, i, i, i, i, f, f, vp, i]
+    lib.gemm_launcher_sub.restype = i
     return lib
 
 
@@ -127,6 +129,26 @@ def gemm(a, b, c, alpha: float = 1.0, beta: float = 0.0, stream=None, path: int 
                                   path, tile_n)
         if rc != 0:
             raise GemmError(f"path {path} / tile_n {tile_n} cannot serve M={m} N={n} K={k}")
+
+
+def gemm_sub(a, b, c, alpha: float = 1.0, beta: float = 0.0, stream=None, max_sms: int = 0) -> None:
+    """C = half(alpha * A@B + beta * C) in place, where A, B, C may be row-strided
+    views (unit column stride, e.g. a column block of a wider C), on at most
+    `max_sms` SMs (0 = all). The dense tcgen05 path of gemm_launcher_sub."""
+    import torch
+    lib = load()
+    for name, t in (("A", a), ("B", b), ("C", c)):
+        if t.dtype != torch.float16 or not t.is_cuda or t.dim() != 2 or t.stride(1) != 1:
+            raise GemmError(f"{name} must be a 2-D CUDA float16 tensor with unit column stride")
+    m, k = a.shape
+    k2, n = b.shape
+    if k2 != k or tuple(c.shape) != (m, n):
+        raise GemmError(f"shape mismatch A{tuple(a.shape)} B{tuple(b.shape)} C{tuple(c.shape)}")
+    rc = lib.gemm_launcher_sub(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), c.data_ptr(),
+                               c.stride(0), m, n, k, alpha, beta, _stream_handle(stream), max_sms)
+    if rc != 0:
+        raise GemmError(f"gemm_launcher_sub refused M={m} N={n} K={k} "
+                        f"(pitches {a.stride(0)}, {b.stride(0)}, {c.stride(0)})")
 
 
 def gemm_tn(a, bt, c, alpha: float = 1.0, beta: float = 0.0, stream=None, tile_n: int = 0) -> None:

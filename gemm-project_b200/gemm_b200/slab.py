@@ -9,8 +9,14 @@ group's backend (NCCL over NVLink/NVSwitch on B200s). Each rank then runs the
 unchanged single-GPU `gemm_launcher_stream` on its slab: no reduction, no
 collective inside a step, no kernel that reads another GPU's memory.
 
-One process per GPU; the group comes from `torch.distributed`. The compute step
-is injectable so the host logic (partition, broadcast, gather) is testable on
+`broadcast_and_run` overlaps that broadcast with the GEMM. B travels as column
+blocks, and each rank computes C[:, block] = A @ B[:, block] as soon as the block
+has landed, while the next blocks are still in flight. Every output element
+still takes its whole K range in one kernel, so the arithmetic is that of the
+plain path. Splitting along K would instead round C to FP16 between blocks.
+
+One process per GPU; the group comes from `torch.distributed`. The compute steps
+are injectable so the host logic (partition, broadcast, gather) is testable on
 CPU ranks with the gloo backend.
 """
 from __future__ import annotations
@@ -21,17 +27,26 @@ import torch
 import torch.distributed as dist
 
 from . import gemm as _gpu_gemm
+from . import gemm_sub as _gpu_gemm_sub
 from . import slab_rows
 
 
 class SlabGemm:
     def __init__(self, group: Optional[dist.ProcessGroup] = None,
-                 compute: Optional[Callable] = None):
+                 compute: Optional[Callable] = None, compute_sub: Optional[Callable] = None,
+                 bcast_group: Optional[dist.ProcessGroup] = None):
         self.group = group
+        # group that carries broadcast_and_run's blocks (see broadcast_group())
+        self.bcast_group = bcast_group if bcast_group is not None else group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         # compute(a_slab, b, c_slab, alpha, beta) -> None (in place on c_slab)
         self.compute = compute or (lambda a, b, c, alpha, beta: _gpu_gemm(a, b, c, alpha, beta))
+        # compute_sub(a_slab, b_block, c_view, alpha, beta, max_sms) -> None, where
+        # c_view is a column block of C (row pitch = C's width)
+        self.compute_sub = compute_sub or (
+            lambda a, b, c, alpha, beta, max_sms: _gpu_gemm_sub(a, b, c, alpha, beta,
+                                                                max_sms=max_sms))
 
     def partition(self, m: int) -> tuple[int, int]:
         """(row0, rows) of this rank's C slab."""
@@ -41,6 +56,53 @@ class SlabGemm:
         """Replicate B from `src` into `b` on every rank (in place), once."""
         dist.broadcast(b, src=src, group=self.group)
         return b
+
+    @staticmethod
+    def broadcast_group(ranks: list[int], max_ctas: int) -> dist.ProcessGroup:
+        """A NCCL group for broadcast_and_run whose collectives use at most
+        `max_ctas` CTAs, on a high-priority stream. With the GEMM leaving that
+        many SMs free, every broadcast CTA finds an SM. Otherwise a ring
+        channel whose CTA cannot be scheduled stalls its peers until the GEMM
+        ends, and the overlap is lost. Collective: every rank calls it."""
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.config.max_ctas = max_ctas
+        opts.config.min_ctas = 1
+        opts.is_high_priority_stream = True
+        return dist.new_group(ranks=ranks, backend="nccl", pg_options=opts)
+
+    def broadcast_and_run(self, a_slab: torch.Tensor, b: torch.Tensor, c_slab: torch.Tensor,
+                          alpha: float = 1.0, beta: float = 0.0, src: int = 0, chunks: int = 8,
+                          reserve_sms: int = 16) -> list[torch.Tensor]:
+        """broadcast_b(b, src) followed by run(...), overlapped.
+
+        B[K, N] (filled on `src`; its contents elsewhere are ignored) is split
+        into `chunks` column blocks. On `src` each block is packed contiguously,
+        and all blocks are broadcast asynchronously in order. Each rank's stream
+        waits for block j, then computes C[:, block j] = alpha * A @ B[:, block j]
+        + beta * C[:, block j] while blocks j+1.. are in flight. Until the last
+        block, the GEMM leaves `reserve_sms` SMs free, because the collective's
+        kernels cannot start while a persistent GEMM holds every SM. Returns the
+        blocks, which hold this rank's replica of B in column-block layout.
+        Ranks must call it collectively with the same chunks."""
+        k, n = b.shape
+        width = -(-n // chunks)
+        bounds = [(c0, min(n, c0 + width)) for c0 in range(0, n, width)]
+        blocks, works = [], []
+        for c0, c1 in bounds:
+            blk = torch.empty((k, c1 - c0), dtype=b.dtype, device=b.device)
+            if self.rank == src:
+                blk.copy_(b[:, c0:c1])
+            works.append(dist.broadcast(blk, src=src, group=self.bcast_group, async_op=True))
+            blocks.append(blk)
+        total_sms = (torch.cuda.get_device_properties(b.device).multi_processor_count
+                     if b.is_cuda else 0)
+        for j, ((c0, c1), blk, work) in enumerate(zip(bounds, blocks, works)):
+            work.wait()  # this stream waits for block j; the host does not block
+            pending = j + 1 < len(bounds)
+            max_sms = max(2, total_sms - reserve_sms) if (pending and total_sms) else 0
+            if a_slab.shape[0]:
+                self.compute_sub(a_slab, blk, c_slab[:, c0:c1], alpha, beta, max_sms)
+        return blocks
 
     def run(self, a_slab: torch.Tensor, b: torch.Tensor, c_slab: torch.Tensor, alpha: float = 1.0,
             beta: float = 0.0) -> None:

@@ -89,6 +89,20 @@ GEMM_API int gemm_launcher_tn(const gemm_half_t* A, const gemm_half_t* Bt, gemm_
 GEMM_API bool launchGemmSample(const gemm_half_t* a, const gemm_half_t* b, gemm_half_t* c, int m,
                                int n, int k, cudaStream_t stream);
 
+/* Dense C = half_rn(alpha * A * B + beta * C) on sub-matrices and part of the
+ * GPU, for the multi-GPU launcher (no counterpart in the reference, which is
+ * single-GPU). A[M,K], B[K,N], C[M,N] are row-major with row pitches lda, ldb,
+ * ldc (elements), so C may be a column block of a wider matrix. max_sms caps the
+ * SMs the tcgen05 kernel occupies (0 = all): the rest stay free for concurrent
+ * kernels such as NCCL's, which cannot start while a persistent kernel holds
+ * every SM. A and B must be TMA-addressable (16-byte aligned bases, lda and ldb
+ * multiples of 8); C may be misaligned (predicated stores). Returns 0, or -1
+ * (nothing launched) for K <= 0, pitches smaller than the widths, or operands
+ * that are not TMA-addressable. Asynchronous on `stream`. */
+GEMM_API int gemm_launcher_sub(const gemm_half_t* A, int lda, const gemm_half_t* B, int ldb,
+                               gemm_half_t* C, int ldc, int M, int N, int K, float alpha,
+                               float beta, cudaStream_t stream, int max_sms);
+
 /* The first launch error recorded on this thread since the last call (a
  * cudaError_t value, 0 if none), cleared by the call. Unlike
  * gemm_launcher_status() it reads no device memory and never synchronizes, so

@@ -38,13 +38,37 @@ def _rank_main(rank, world, port, scenario, q):
         dist.init_process_group("gloo", rank=rank, world_size=world,
                                 timeout=timedelta(seconds=5))
         m, n, k, alpha, beta = 37, 24, 40, 0.75, -0.25
+        if scenario == "overlapped":
+            n = 26  # three column blocks of 9, 9 and 8
         a, b_full, c = oracle.make_inputs(m, n, k, "uniform", seed=11)
 
         def cpu_compute(a_s, b_s, c_s, al, be):
             c_s.copy_(oracle.c_gemm(a_s, b_s, c_s, al, be))
 
-        sg = SlabGemm(compute=cpu_compute)
+        def cpu_compute_sub(a_s, b_s, c_v, al, be, max_sms):  # c_v: a column block of C
+            c_v.copy_(oracle.c_gemm(a_s, b_s.contiguous(), c_v.contiguous(), al, be))
+
+        sg = SlabGemm(compute=cpu_compute, compute_sub=cpu_compute_sub)
         row0, rows = sg.partition(m)
+        if scenario == "overlapped":
+            b = b_full.clone() if rank == 0 else torch.full_like(b_full, float("nan"))
+            a_slab = a[row0:row0 + rows].contiguous()
+            c_slab = c[row0:row0 + rows].clone()
+            blocks = sg.broadcast_and_run(a_slab, b, c_slab, alpha, beta, chunks=3)
+            assert [t.shape[1] for t in blocks] == [9, 9, 8]
+            assert torch.equal(torch.cat(blocks, dim=1), b_full)
+            plain = c[row0:row0 + rows].clone()
+            cpu_compute(a_slab, b_full, plain, alpha, beta)
+            assert torch.equal(c_slab, plain), "column blocks change the arithmetic"
+            full = sg.gather_c(c_slab, m)
+            if rank == 0:
+                chk = oracle.check(full, oracle.reference_fp32(a, b_full, c, alpha, beta))
+                q.put((rank, "ok" if chk.passed else f"mismatch {chk}", rows, row0))
+            else:
+                q.put((rank, "ok", rows, row0))
+            dist.barrier()
+            dist.destroy_process_group()
+            return
         if scenario == "die_before_broadcast" and rank == 1:
             os._exit(3)  # this rank disappears without joining the collective
         b = b_full.clone() if rank == 0 else torch.zeros_like(b_full)
@@ -98,6 +122,13 @@ def test_slab_gemm_two_ranks_matches_oracle():
     # M = 37 over 2 ranks: 19 + 18 rows, remainder on rank 0
     assert (results[0][2], results[0][3]) == (19, 0)
     assert (results[1][2], results[1][3]) == (18, 19)
+
+
+def test_overlapped_broadcast_two_ranks_matches_plain_path():
+    """B broadcast as column blocks, each consumed as it lands (broadcast_and_run)."""
+    results, alive = _spawn(2, "overlapped")
+    assert not alive, "a rank hung"
+    assert [r[1] for r in results] == ["ok", "ok"], results
 
 
 def test_dead_rank_surfaces_as_error_not_hang():
