@@ -1,4 +1,4 @@
-// Small-M ("decode") GEMM on tcgen05 for sm_100a: C[M <= 64, N] with
+// Small-M ("decode") GEMM on tcgen05 for sm_100a: C[M <= 256, N] with
 // TMA-addressable A and B.
 //
 // The reference serves 2 <= M < 64 with mma.sync kernels whose 16- or 32-row
@@ -16,6 +16,10 @@
 // The epilogue stores C[m][n] with lanes on consecutive n (64-byte runs).
 // Warp roles as in the dense kernel: warp 0 TMA producer, warp 1 TMEM owner
 // and UMMA issuer, warps 2..5 epilogue. Every wait is bounded.
+// For 64 < M <= 256 the dense kernel would have too few output tiles to fill
+// the GPU (one tile row), while this kernel's tiles are 128 output columns
+// with the K range split over a cluster, so it serves that range too (UMMA
+// N = 128 or 256).
 #pragma once
 
 #include "ptx.cuh"
@@ -24,14 +28,15 @@ namespace gemm_b200 {
 
 template <int NM_>
 struct DecCfg {
-  static constexpr int NM = NM_;                    // UMMA N = M padded (16, 32, 64)
+  static constexpr int NM = NM_;                    // UMMA N = M padded (16 ... 256)
   static constexpr int BMN = 128;                   // output columns per tile (UMMA M)
   static constexpr int BK = 64;
   static constexpr int kBBoxBytes = 64 * BK * 2;    // 64 columns x 64 K of B
   static constexpr int kBBytes = BMN * BK * 2;      // 16 KiB
   static constexpr int kABytes = NM * BK * 2;       // NM rows x 64 K of A
   static constexpr int kStageBytes = kBBytes + kABytes;
-  static constexpr int kStages = NM >= 32 ? 4 : 5;  // ring <= 96 KiB: two CTAs per SM
+  // ring <= 96 KiB for NM <= 64 (two CTAs per SM); one CTA per SM above
+  static constexpr int kStages = NM >= 32 ? 4 : 5;
   // two accumulators (even / odd K steps) halve the chain of dependent UMMAs
   static constexpr int kTmemCols = 2 * NM < 32 ? 32 : 2 * NM;
   static constexpr int kPartBytes = NM * BMN * 4;   // FP32 partial for the cluster reduction
@@ -40,7 +45,9 @@ struct DecCfg {
   static constexpr int kSmemBytes =
       (kRingBytes > kPartBytes ? kRingBytes : kPartBytes) + kBarBytes + 1024;
   static constexpr int kThreads = 192;
-  static_assert(NM == 16 || NM == 32 || NM == 64, "UMMA N");
+  static constexpr int kChunk = NM < 32 ? NM : 32;  // TMEM columns per epilogue load
+  static_assert(NM == 16 || NM == 32 || NM == 64 || NM == 128 || NM == 256, "UMMA N");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
 struct DecParams {
@@ -53,9 +60,9 @@ struct DecParams {
   int* err;
 };
 
-template <int NM>
+template <int NC>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t* r) {
-  if constexpr (NM == 16) {
+  if constexpr (NC == 16) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -66,7 +73,7 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t* r) {
         : "memory");
   } else {
 #pragma unroll
-    for (int i = 0; i < NM / 32; ++i)
+    for (int i = 0; i < NC / 32; ++i)
       tmem_ld_32x32b_x32(taddr + 32 * i, *reinterpret_cast<uint32_t(*)[32]>(r + 32 * i));
   }
 }
@@ -171,26 +178,42 @@ __global__ void __launch_bounds__(DecCfg<NM>::kThreads, 1)
   }
 
   // ---------------- epilogue: warps 2..5 own TMEM lane quadrants ----------------
+  // The two accumulators (even / odd K steps) are summed kChunk columns (= output
+  // rows m) at a time. Without a split the sums go straight to C; with one they
+  // go to part[m][128] in this CTA's shared memory (the ring is idle by then:
+  // every stage has been consumed), for the cluster reduction below.
   const bool epi = warp >= 2;
   const int quad = warp & 3;
   const int n = n0 + quad * 32 + lane;
-  uint32_t r[NM];
-  bool have = false;
+  const bool read_c = p.beta != 0.0f;
+  const int mmax = min(p.M, NM);
+  float* part = reinterpret_cast<float*>(smem);
   if (epi) {
-    if (num_kb > 0 &&
-        mbar_wait_warp(done_bar, 0, p.timeout_ns, abort_flag, p.err, kErrTimeoutEpilogue)) {
-      tc_fence_after();
-      uint32_t r2[NM];
-      tmem_ld_cols<NM>(tmem_base + (static_cast<uint32_t>(quad * 32) << 16), r);
-      tmem_ld_cols<NM>(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + NM, r2);
-      tmem_wait_ld();
+    const bool have = num_kb > 0 && mbar_wait_warp(done_bar, 0, p.timeout_ns, abort_flag, p.err,
+                                                   kErrTimeoutEpilogue);
+    if (have) tc_fence_after();
+    const uint32_t t0 = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
 #pragma unroll
-      for (int m = 0; m < NM; ++m) r[m] = __float_as_uint(__uint_as_float(r[m]) + __uint_as_float(r2[m]));
-      have = true;
-    }
-    if (!have) {
+    for (int i = 0; i < NM / Cfg::kChunk; ++i) {
+      uint32_t r[Cfg::kChunk], r2[Cfg::kChunk];
+      if (have) {
+        tmem_ld_cols<Cfg::kChunk>(t0 + i * Cfg::kChunk, r);
+        tmem_ld_cols<Cfg::kChunk>(t0 + NM + i * Cfg::kChunk, r2);
+        tmem_wait_ld();
+      }
 #pragma unroll
-      for (int m = 0; m < NM; ++m) r[m] = 0u;  // empty K range contributes zero
+      for (int j = 0; j < Cfg::kChunk; ++j) {
+        // an empty K range (a cluster rank past K) contributes zero
+        const float v = have ? __uint_as_float(r[j]) + __uint_as_float(r2[j]) : 0.0f;
+        const int m = i * Cfg::kChunk + j;
+        if (p.ksplit > 1) {
+          part[m * Cfg::BMN + quad * 32 + lane] = v;
+        } else if (m < mmax && n < p.N) {
+          half* dst = p.C + static_cast<size_t>(m) * p.N + n;
+          const float prev = read_c ? __half2float(*dst) : 0.0f;
+          *dst = __float2half_rn(fmaf(p.alpha, v, p.beta * prev));
+        }
+      }
     }
   }
   tc_fence_before();
@@ -199,30 +222,9 @@ __global__ void __launch_bounds__(DecCfg<NM>::kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
+  if (p.ksplit == 1) return;
 
-  const bool read_c = p.beta != 0.0f;
-  const int mmax = min(p.M, NM);
-  if (p.ksplit == 1) {
-    if (epi && n < p.N) {
-#pragma unroll
-      for (int m = 0; m < NM; ++m) {
-        if (m < mmax) {
-          half* dst = p.C + static_cast<size_t>(m) * p.N + n;
-          const float prev = read_c ? __half2float(*dst) : 0.0f;
-          *dst = __float2half_rn(fmaf(p.alpha, __uint_as_float(r[m]), p.beta * prev));
-        }
-      }
-    }
-    return;
-  }
-
-  // Cluster split-K: partials as part[m][128] in this CTA's smem (the ring is
-  // idle: every stage has been consumed), then rank q finalises a slice of n.
-  float* part = reinterpret_cast<float*>(smem);
-  if (epi) {
-#pragma unroll
-    for (int m = 0; m < NM; ++m) part[m * Cfg::BMN + quad * 32 + lane] = __uint_as_float(r[m]);
-  }
+  // Cluster split-K: rank q finalises a slice of n from every rank's partials.
   cluster_sync_all();
   const int rank = static_cast<int>(cluster_ctarank());
   const int span = Cfg::BMN / p.ksplit;

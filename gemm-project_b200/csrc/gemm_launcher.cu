@@ -9,6 +9,7 @@
 //   K <= 0                      -> scale_c_kernel (C = beta*C)
 //   M == 1                      -> rows_tma_kernel<1>    (TMA-fed HBM streaming, cluster split-K)
 //   2 <= M <= 64, TMA-friendly  -> skinny_tc_kernel<NM>  (tcgen05, C^T = B^T A^T, cluster split-K)
+//   64 < M <= 256, N <= 8192, long K, TMA-friendly -> skinny_tc_kernel<128|256>
 //   M <= 8 otherwise            -> rows_gemv_kernel<MR>  (per-thread loads, any alignment)
 //   N == 1                      -> col_tma_kernel / col_gemv_kernel
 //   otherwise                   -> tc_gemm_kernel<...>   (tcgen05 + TMA + TMEM tiles)
@@ -68,7 +69,7 @@ struct DeviceInfo {
   int pair2_clusters = 0;         // co-resident 2-CTA clusters, 512 x 256 pair tiles
   int pairn_clusters = 0;         // co-resident 2-CTA clusters, 256 x 512 pair tiles
   int stream_slots = 0;           // co-resident CTAs of the TMA streaming kernels
-  int dec_slots[3] = {0, 0, 0};   // co-resident CTAs of skinny_tc_kernel<16|32|64>
+  int dec_slots[5] = {0, 0, 0, 0, 0};  // co-resident CTAs of skinny_tc_kernel<16|32|64|128|256>
   int* err = nullptr;
   cudaMemPool_t pool = nullptr;   // repack scratch (never trimmed between calls)
   bool configured = false;
@@ -204,6 +205,10 @@ DeviceInfo& device_info() {
                            DecCfg<32>::kSmemBytes);
       cudaFuncSetAttribute(skinny_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            DecCfg<64>::kSmemBytes);
+      cudaFuncSetAttribute(skinny_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           DecCfg<128>::kSmemBytes);
+      cudaFuncSetAttribute(skinny_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           DecCfg<256>::kSmemBytes);
       // Capacity from the shared-memory budget (228 KiB per SM, 1 KiB reserved
       // per CTA), at most two CTAs per SM: the occupancy query reports one CTA
       // per SM for these TMEM-allocating kernels, while two co-resident CTAs
@@ -215,6 +220,8 @@ DeviceInfo& device_info() {
       d.dec_slots[0] = slots(DecCfg<16>::kSmemBytes);
       d.dec_slots[1] = slots(DecCfg<32>::kSmemBytes);
       d.dec_slots[2] = slots(DecCfg<64>::kSmemBytes);
+      d.dec_slots[3] = slots(DecCfg<128>::kSmemBytes);
+      d.dec_slots[4] = slots(DecCfg<256>::kSmemBytes);
     }
     {
       cudaMemPoolProps props{};
@@ -734,16 +741,30 @@ int launch_col_tma(const half* A, const half* B, half* C, int M, int K, float al
 // ---------------------------------------------------------------------------
 // Small-M tensor-core path (2 <= M <= 64, TMA-addressable operands).
 // ---------------------------------------------------------------------------
+// For 64 < M <= 256 the dense tiles leave the GPU under-filled when N is
+// modest (one tile row, few tile columns, every tile looping over all of K); the
+// small-M kernel splits K over a cluster instead. Measured on B200, it wins by
+// 1.4-2.9x when N <= 8192 and K >= 2048 (M <= 128) or K >= 8192 (M <= 256), and
+// loses for wide N or short K.
+bool small_m_wins(int M, int N, int K) {
+  return M <= 256 && N <= 8192 && (M <= 128 ? K >= 2048 : K >= 8192);
+}
+
 bool dec_ok(const half* A, const half* B, int M, int N, int K, const DeviceInfo& d) {
-  return d.dec_slots[0] > 0 && M >= 1 && M <= 64 && aligned16(A) && aligned16(B) && K % 8 == 0 &&
+  return d.dec_slots[0] > 0 && M >= 1 && M <= 256 && aligned16(A) && aligned16(B) && K % 8 == 0 &&
          N % 8 == 0;
+}
+
+constexpr int dec_index(int nm) {
+  return nm == 16 ? 0 : (nm == 32 ? 1 : (nm == 64 ? 2 : (nm == 128 ? 3 : 4)));
 }
 
 template <int NM>
 void launch_dec_nm(const CUtensorMap& ta, const CUtensorMap& tb, const DecParams& p, int tiles,
                    cudaStream_t s, int M, int N, int K) {
-  static const char* names[3] = {"skinny_tc_kernel<16>", "skinny_tc_kernel<32>",
-                                 "skinny_tc_kernel<64>"};
+  static const char* names[5] = {"skinny_tc_kernel<16>", "skinny_tc_kernel<32>",
+                                 "skinny_tc_kernel<64>", "skinny_tc_kernel<128>",
+                                 "skinny_tc_kernel<256>"};
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(tiles, p.ksplit, 1);
   cfg.blockDim = dim3(DecCfg<NM>::kThreads, 1, 1);
@@ -756,13 +777,13 @@ void launch_dec_nm(const CUtensorMap& ta, const CUtensorMap& tb, const DecParams
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  log_launch(names[NM == 16 ? 0 : (NM == 32 ? 1 : 2)], M, N, K, cfg.gridDim, cfg.blockDim);
+  log_launch(names[dec_index(NM)], M, N, K, cfg.gridDim, cfg.blockDim);
   record_error(cudaLaunchKernelEx(&cfg, skinny_tc_kernel<NM>, ta, tb, p));
 }
 
 int launch_dec(const half* A, const half* B, half* C, int M, int N, int K, float alpha,
                float beta, cudaStream_t s, const DeviceInfo& d) {
-  const int nm = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+  const int nm = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256)));
   CUtensorMap ta, tb;
   if (!(make_tmap(&tb, B, N, K, static_cast<uint64_t>(N) * 2, 64, 64) &&
         make_tmap(&ta, A, K, M, static_cast<uint64_t>(K) * 2, 64, nm))) {
@@ -770,7 +791,7 @@ int launch_dec(const half* A, const half* B, half* C, int M, int N, int K, float
     return -1;
   }
   const int tiles = ceil_div(N, 128);
-  const int slots = d.dec_slots[nm == 16 ? 0 : (nm == 32 ? 1 : 2)];
+  const int slots = d.dec_slots[dec_index(nm)];
   int ksplit = 1;
   while (ksplit < 8 && tiles * ksplit * 2 <= slots && K / (ksplit * 2) >= 256) ksplit *= 2;
   const int forced_ks = env_int("GEMM_DEC_KSPLIT");
@@ -789,7 +810,9 @@ int launch_dec(const half* A, const half* B, half* C, int M, int N, int K, float
   switch (nm) {
     case 16: launch_dec_nm<16>(ta, tb, p, tiles, s, M, N, K); break;
     case 32: launch_dec_nm<32>(ta, tb, p, tiles, s, M, N, K); break;
-    default: launch_dec_nm<64>(ta, tb, p, tiles, s, M, N, K); break;
+    case 64: launch_dec_nm<64>(ta, tb, p, tiles, s, M, N, K); break;
+    case 128: launch_dec_nm<128>(ta, tb, p, tiles, s, M, N, K); break;
+    default: launch_dec_nm<256>(ta, tb, p, tiles, s, M, N, K); break;
   }
   return 0;
 }
@@ -808,7 +831,7 @@ int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float a
   if (path == 0) {
     if (M == 1)
       path = 2;                       // streaming GEMV
-    else if (M <= 64 && N > 1 && dec_ok(A, B, M, N, K, d))
+    else if (N > 1 && dec_ok(A, B, M, N, K, d) && (M <= 64 || small_m_wins(M, N, K)))
       path = 6;                       // small-M tensor-core kernel
     else if (M <= 8)
       path = 2;                       // misaligned small M: per-thread loads

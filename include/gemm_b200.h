@@ -56,7 +56,7 @@ GEMM_API void gemm_launcher_stream(const gemm_half_t* A, const gemm_half_t* B, g
  * 3 = column kernel (N == 1; TMA-fed when the operands allow),
  * 4 = multi-row kernel with per-thread loads, 5 = column kernel with
  * per-thread loads (the paths misaligned operands take), 6 = small-M
- * tensor-core kernel (M <= 64, 16-byte aligned A and B, K % 8 == 0, N % 8 == 0).
+ * tensor-core kernel (M <= 256, 16-byte aligned A and B, K % 8 == 0, N % 8 == 0).
  * tile_n (path 1): 0 = automatic; 64, 128 or 256 = one CTA per 128 x tile_n
  * output tile (tcgen05.mma.cta_group::1); 2 = a 2-CTA cluster per 256 x 256
  * output tile (tcgen05.mma.cta_group::2); 3 = a 2-CTA cluster per 512 x 256

@@ -93,7 +93,10 @@ def test_col_path(lib, cuda, shape, offset, path):
 
 @pytest.mark.parametrize("shape", [(2, 264, 296), (8, 6144, 4096), (16, 1024, 18944), (17, 640, 672),
                                    (32, 6144, 4096), (33, 2056, 1000), (64, 512, 64), (5, 8, 8),
-                                   (3, 5000, 4096), (48, 4104, 2000), (64, 28672, 8192)], ids=str)
+                                   (3, 5000, 4096), (48, 4104, 2000), (64, 28672, 8192),
+                                   (65, 4096, 4096), (128, 4096, 4096), (129, 1000, 520),
+                                   (200, 2048, 8192), (256, 512, 64), (256, 28672, 1024),
+                                   (97, 8, 8)], ids=str)
 def test_small_m_tensor_core_path(lib, cuda, shape):
     m, n, k = shape
     _go(lib, cuda, m, n, k, 0.75, -0.5, dist="normal", path=PATH_DEC, seed=m + n)
@@ -215,3 +218,10 @@ def test_dispatch_choices(lib, cuda):
     assert names[(3, 5000, 4097)].startswith("rows_gemv_kernel<4")
     run(lib, cuda, 8, 6144, 4096, fn="launcher")
     assert gemm_b200.last_kernel().startswith("skinny_tc_kernel<16>")
+    # 64 < M <= 256: the split-K small-M kernel for modest N and long K, dense otherwise
+    run(lib, cuda, 128, 4096, 4096, fn="launcher")
+    assert gemm_b200.last_kernel().startswith("skinny_tc_kernel<128>")
+    run(lib, cuda, 200, 4096, 8192, fn="launcher")
+    assert gemm_b200.last_kernel().startswith("skinny_tc_kernel<256>")
+    run(lib, cuda, 128, 14336, 4096, fn="launcher")
+    assert gemm_b200.last_kernel().startswith("tc_gemm_kernel")
