@@ -9,7 +9,7 @@
 //   K <= 0                      -> scale_c_kernel (C = beta*C)
 //   M == 1                      -> rows_tma_kernel<1>    (TMA-fed HBM streaming, cluster split-K)
 //   2 <= M <= 64, TMA-friendly  -> skinny_tc_kernel<NM>  (tcgen05, C^T = B^T A^T, cluster split-K)
-//   64 < M <= 256, N <= 8192, long K, TMA-friendly -> skinny_tc_kernel<128|256>
+//   64 < M <= 128, K >= 3N, TMA-friendly            -> skinny_tc_kernel<128>
 //   M <= 8 otherwise            -> rows_gemv_kernel<MR>  (per-thread loads, any alignment)
 //   N == 1                      -> col_tma_kernel / col_gemv_kernel
 //   otherwise                   -> tc_gemm_kernel<...>   (tcgen05 + TMA + TMEM tiles)
@@ -307,6 +307,30 @@ void launch_scale(half* C, int M, int N, float beta, cudaStream_t s, const Devic
 constexpr int kTilePair = 2;
 constexpr int kTilePair2 = 3;
 constexpr int kTilePairN = 4;
+// kTileSplitK = 128 x 256 single-CTA tiles with the K range split over a
+// cluster of 2, 4 or 8 CTAs (a request for tests; the automatic choice applies
+// split_k_plan()).
+constexpr int kTileSplitK = 5;
+
+// Split-K for small and mid-size problems: when 128 x 256 tiles are too few to
+// fill the GPU, the K range of each tile is split over a cluster (DSMEM
+// reduction). Larger tiles with split-K move far less data through L2 than many
+// small tiles: 1.4-1.7x faster for long K (e.g. 256x4096x4096: 17 instead of
+// 29 us), slower for short K, so each part keeps at least 16 K blocks.
+// Every K part holds at least one K block (num_kb > ks * (ks - 1) guarantees
+// it). GEMM_SPLITK=-1 turns it off.
+int split_k_plan(int M, int N, int K, const DeviceInfo& d) {
+  if (env_int("GEMM_SPLITK") < 0) return 1;
+  const int tiles = ceil_div(M, 128) * ceil_div(N, 256);
+  const int num_kb = ceil_div(K, 64);
+  int ks = 1;
+  // at least 16 K blocks per part: with shorter parts the per-CTA start-up and
+  // the cluster reduction cost more than the split saves (measured at 1024^3)
+  while (ks < 8 && tiles * ks * 2 <= d.sms && num_kb >= 2 * ks * 16 &&
+         num_kb > 2 * ks * (2 * ks - 1))
+    ks *= 2;
+  return ks;
+}
 
 bool tile_available(int tile, const DeviceInfo& d) {
   return tile == 64 || tile == 128 || tile == 256 || (tile == kTilePair && d.pair_clusters > 0) ||
@@ -389,6 +413,23 @@ void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     log_launch(name, M, N, K, cfg.gridDim, cfg.blockDim);
     record_error(
         cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, true, BKM, SLABS, SLAB_N>, ta, tb, tc, p));
+  } else if (p.ksplit > 1) {
+    // split-K: one CTA per (tile, K part), the parts of a tile in one cluster
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(tiles, p.ksplit, 1);
+    cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = p.ksplit;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    log_launch(name, M, N, K, cfg.gridDim, cfg.blockDim);
+    record_error(
+        cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, false, BKM, SLABS, SLAB_N>, ta, tb, tc, p));
   } else {
     const int grid = std::min(tiles, max_sms > 0 ? std::min(d.sms, max_sms) : d.sms);
     log_launch(name, M, N, K, dim3(grid), dim3(Cfg::kThreads));
@@ -403,7 +444,7 @@ void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
 // b_kmajor: B is given as Bt[N,K] (row pitch ldb), i.e. C = A * Bt^T.
 int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half* C, int M, int N,
                    int K, float alpha, float beta, cudaStream_t s, int tile, const DeviceInfo& d,
-                   bool b_kmajor = false, int ldc = 0, int max_sms = 0) {
+                   bool b_kmajor = false, int ldc = 0, int max_sms = 0, int ksplit = 1) {
   if (ldc <= 0) ldc = N;
   const bool pair = tile == kTilePair || tile == kTilePair2 || tile == kTilePairN;
   const int slabs = tile == kTilePair2 ? 2 : 1;  // A slabs per CTA
@@ -443,6 +484,12 @@ int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half*
   p.c_vec_ok = aligned16(C) && ldc % 8 == 0;
   p.timeout_ns = wait_timeout_ns();
   p.err = d.err;
+  p.ksplit = 1;
+  p.kb_per = p.num_kb;
+  if (ksplit > 1 && !pair) {
+    p.ksplit = ksplit;
+    p.kb_per = ceil_div(p.num_kb, ksplit);
+  }
   if (b_kmajor) {
     switch (tile) {
       case 64: launch_tc_bn<64, false, true, 1>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
@@ -514,6 +561,17 @@ void repack_operands(const half* A, const half* B, int M, int N, int K, cudaStre
 
 int launch_tc(const half* A, const half* B, half* C, int M, int N, int K, float alpha, float beta,
               cudaStream_t s, int tile, const DeviceInfo& d) {
+  int ksplit = 1;
+  if (tile == 0 || tile == kTileSplitK) {
+    ksplit = split_k_plan(M, N, K, d);
+    if (tile == kTileSplitK) {
+      const int num_kb = ceil_div(K, 64);
+      if (ksplit == 1 && num_kb > 2) ksplit = 2;  // a forced request splits at least in two
+      tile = 256;
+    } else if (ksplit > 1) {
+      tile = 256;
+    }
+  }
   if (tile != 0 && !tile_available(tile, d)) tile = 256;
   if (tile == 0) tile = choose_tile(M, N, d);
   const size_t need = repack_bytes(A, B, M, N, K);
@@ -533,7 +591,8 @@ int launch_tc(const half* A, const half* B, half* C, int M, int N, int K, float 
     static const char* const names[2] = {"pack_rows_kernel<A>", "pack_rows_kernel<B>"};
     repack_operands(A, B, M, N, K, s, d, scratch, names, &a_src, &lda, &b_src, &ldb);
   }
-  const int rc = launch_tc_core(a_src, lda, b_src, ldb, C, M, N, K, alpha, beta, s, tile, d);
+  const int rc = launch_tc_core(a_src, lda, b_src, ldb, C, M, N, K, alpha, beta, s, tile, d,
+                                /*b_kmajor=*/false, /*ldc=*/0, /*max_sms=*/0, ksplit);
   if (scratch) cudaFreeAsync(scratch, s);
   return rc;
 }
@@ -741,13 +800,13 @@ int launch_col_tma(const half* A, const half* B, half* C, int M, int K, float al
 // ---------------------------------------------------------------------------
 // Small-M tensor-core path (2 <= M <= 64, TMA-addressable operands).
 // ---------------------------------------------------------------------------
-// For 64 < M <= 256 the dense tiles leave the GPU under-filled when N is
-// modest (one tile row, few tile columns, every tile looping over all of K); the
-// small-M kernel splits K over a cluster instead. Measured on B200, it wins by
-// 1.4-2.9x when N <= 8192 and K >= 2048 (M <= 128) or K >= 8192 (M <= 256), and
-// loses for wide N or short K.
+// For 64 < M <= 128 the dense path (128 x 256 tiles, split-K in a cluster when
+// the tiles are few) is faster, except when K is long against N: there the
+// small-M kernel's 128-column tiles give more CTAs (measured on B200: at
+// 96 x 4096 x 14336, 37 against 47 us; at 128 x 4096 x 4096, 23 against 16 us the
+// other way). Above M = 128 the dense path wins throughout.
 bool small_m_wins(int M, int N, int K) {
-  return M <= 256 && N <= 8192 && (M <= 128 ? K >= 2048 : K >= 8192);
+  return M <= 128 && static_cast<long long>(K) >= 3ll * N;
 }
 
 bool dec_ok(const half* A, const half* B, int M, int N, int K, const DeviceInfo& d) {
@@ -826,7 +885,7 @@ int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float a
     return 0;
   }
   if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256 && tile_n != kTilePair &&
-      tile_n != kTilePair2 && tile_n != kTilePairN)
+      tile_n != kTilePair2 && tile_n != kTilePairN && tile_n != kTileSplitK)
     return -1;
   if (path == 0) {
     if (M == 1)

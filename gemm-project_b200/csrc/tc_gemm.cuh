@@ -139,6 +139,12 @@ struct TcParams {
   int c_vec_ok;          // C base 16B-aligned and ldc % 8 == 0 (LSU fallback)
   unsigned long long timeout_ns;
   int* err;
+  // Split-K inside a cluster (single-CTA tiles only; ksplit = 1 otherwise):
+  // the grid is (tiles, ksplit) with clusters of (1, ksplit, 1); CTA y takes K
+  // blocks [y * kb_per, (y + 1) * kb_per), and the cluster adds its FP32
+  // partials through distributed shared memory before writing C.
+  int ksplit;
+  int kb_per;
 };
 
 // Grouped raster over output tiles so that concurrently resident CTAs share A
@@ -327,6 +333,9 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
   const int num_tiles = p.tiles_m * p.tiles_n;
   const int unit = PAIR ? static_cast<int>(blockIdx.x / 2) : static_cast<int>(blockIdx.x);
   const int num_units = PAIR ? static_cast<int>(gridDim.x / 2) : static_cast<int>(gridDim.x);
+  // K blocks of this CTA: all of them, or one part of a cluster split
+  const int kb_lo = p.ksplit > 1 ? static_cast<int>(blockIdx.y) * p.kb_per : 0;
+  const int kb_hi = p.ksplit > 1 ? min(p.num_kb, kb_lo + p.kb_per) : p.num_kb;
 
   if (warp < Cfg::kEpiWarp0) {
     // Control warps (warpgroup 0 for the 256x512 tile): producer, UMMA issuer
@@ -343,7 +352,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
           tile_coords(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
           const int m0 = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kCtaRows;
           const int n0 = tn * Cfg::kTileN + static_cast<int>(rank) * Cfg::kBCols;
-          for (int kb = 0; kb < p.num_kb; ++kb) {
+          for (int kb = kb_lo; kb < kb_hi; ++kb) {
             if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag, p.err,
                            kErrTimeoutProducer)) {
               ok = false;
@@ -385,7 +394,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
         uint32_t acc_phase = 0;
         bool ok = true;
         for (int t = unit; t < num_tiles && ok; t += num_units) {
-          for (int kb = 0; kb < p.num_kb && ok; ++kb) {
+          for (int kb = kb_lo; kb < kb_hi && ok; ++kb) {
             if (!mbar_wait_warp(full_bar(stage), phase, p.timeout_ns, abort_flag, p.err,
                                 kErrTimeoutMma)) {
               ok = false;
@@ -397,7 +406,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
             if constexpr (SLAB_N) {
               // Both N slabs take the same A: fill the A collector on slab 0 and
               // reuse it on slab 1. Both accumulators must be free before kb 0.
-              if (kb == 0) {
+              if (kb == kb_lo) {
   #pragma unroll
                 for (int sl = 0; sl < SLABS; ++sl)
                   if (ok && !mbar_wait_warp(tempty_bar(acc, sl), acc_phase ^ 1u, p.timeout_ns,
@@ -409,7 +418,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
   #pragma unroll
               for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
                 const uint64_t adesc = make_smem_desc(a_addr + kk * 32, 16, 1024);
-                const uint32_t en = (kb | kk) != 0 ? 1u : 0u;
+                const uint32_t en = (kb != kb_lo || kk != 0) ? 1u : 0u;
                 const uint32_t d0 = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
                 const uint64_t b0 = BKM ? make_smem_desc(b_addr + kk * 32, 16, 1024)
                                         : make_smem_desc(b_addr + kk * 2048, Cfg::kBBoxBytes, 1024);
@@ -423,7 +432,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
                 }
                 __syncwarp();
               }
-              if (kb == p.num_kb - 1) {
+              if (kb == kb_hi - 1) {
                 if (elect_one()) {
   #pragma unroll
                   for (int sl = 0; sl < SLABS; ++sl) umma_commit_to<PAIR>(tfull_bar(acc, sl));
@@ -433,7 +442,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
             } else {
   #pragma unroll
               for (int sl = 0; sl < SLABS; ++sl) {
-                if (kb == 0) {
+                if (kb == kb_lo) {
                   // this slab's accumulator must have been drained by the epilogue
                   if (!mbar_wait_warp(tempty_bar(acc, sl), acc_phase ^ 1u, p.timeout_ns, abort_flag,
                                       p.err, kErrTimeoutMma)) {
@@ -457,10 +466,10 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
                       BKM ? make_smem_desc(b_addr + kk * 32, 16, 1024)
                           : make_smem_desc(b_addr + kk * 2048, Cfg::kBBoxBytes, 1024);
                   if (elect_one())
-                    umma_f16<PAIR>(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+                    umma_f16<PAIR>(d_tmem, adesc, bdesc, idesc, (kb != kb_lo || kk != 0) ? 1u : 0u);
                   __syncwarp();
                 }
-                if (kb == p.num_kb - 1) {
+                if (kb == kb_hi - 1) {
                   if (elect_one()) umma_commit_to<PAIR>(tfull_bar(acc, sl));
                   __syncwarp();
                 }
@@ -628,8 +637,9 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
           const int row_base = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kCtaRows +
                                sl * Cfg::BM + quad * 32;
           const int col_base = tn * Cfg::kTileN + col_half * Cfg::kEpiCols;
-          // Prefetch this slab's first two C boxes while its UMMAs still run.
-          if (p.c_tma && read_c && lane == 0) {
+          // Prefetch this slab's first two C boxes while its UMMAs still run
+          // (not with split-K, whose cluster reduction reads C itself).
+          if (p.c_tma && read_c && lane == 0 && (PAIR || p.ksplit <= 1)) {
             bulk_wait_read<0>();  // earlier TMA stores have finished reading both buffers
             issue_c_load(ctr, col_base, row_base);
             if (kChunks > 1) issue_c_load(ctr + 1, col_base + Cfg::kEpiChunk, row_base);
@@ -640,6 +650,28 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
             break;
           }
           tc_fence_after();
+          if (!PAIR && p.ksplit > 1) {
+            // Split-K: this CTA's FP32 partial of the tile into the idle stage
+            // ring, rows padded by 4 floats (bank-conflict-free float4 rows);
+            // the cluster reduction after the role branches writes C.
+            float* part = reinterpret_cast<float*>(smem);
+            const int row = quad * 32 + lane;
+            const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                    static_cast<uint32_t>(col_half * Cfg::kEpiCols);
+  #pragma unroll
+            for (int i = 0; i < kChunks; ++i) {
+              uint32_t r[32];
+              tmem_ld_32x32b_x32(t_addr + i * 32, r);
+              tmem_wait_ld();
+              float4* dst = reinterpret_cast<float4*>(part + row * (BN + 4) + col_half * Cfg::kEpiCols +
+                                                      i * 32);
+  #pragma unroll
+              for (int j = 0; j < 8; ++j)
+                dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                     __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            }
+            continue;
+          }
           // Whole share of the slab into registers, then hand TMEM back at once.
           uint32_t r[Cfg::kEpiCols];
           const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
@@ -728,7 +760,58 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
   if constexpr (PAIR) {
     cluster_sync_all();  // no CTA leaves while its peer may still signal it
   } else {
-    __syncthreads();
+    if (p.ksplit > 1) {
+      // Split-K reduction: every CTA of the cluster holds a partial of the same
+      // tile; CTA q adds all partials for its slice of rows through DSMEM and
+      // writes those rows of C (4 columns per thread step, 8-byte stores).
+      cluster_sync_all();  // all partials written and visible
+      const float* part = reinterpret_cast<const float*>(smem);
+      const int q = static_cast<int>(cluster_ctarank());
+      const int rows = Cfg::BM / p.ksplit;
+      int tm, tn;
+      tile_coords(unit, p.tiles_m, p.tiles_n, p.group, tm, tn);
+      const bool read_c = p.beta != 0.0f;
+      for (int i = threadIdx.x; i < rows * (BN / 4); i += blockDim.x) {
+        const int r = q * rows + i / (BN / 4);
+        const int c4 = i % (BN / 4);
+        const uint32_t local = smem_u32(part + r * (BN + 4) + 4 * c4);
+        float4 sum = ld_shared_cluster_v4(mapa_shared(local, 0));
+        for (int k = 1; k < p.ksplit; ++k) {
+          const float4 v = ld_shared_cluster_v4(mapa_shared(local, static_cast<uint32_t>(k)));
+          sum.x += v.x;
+          sum.y += v.y;
+          sum.z += v.z;
+          sum.w += v.w;
+        }
+        const int row = tm * Cfg::kTileM + r;
+        const int col = tn * Cfg::kTileN + 4 * c4;
+        if (row >= p.M) continue;
+        half* dst = p.C + static_cast<size_t>(row) * p.ldc + col;
+        const float s4[4] = {sum.x, sum.y, sum.z, sum.w};
+        if (p.c_vec_ok && col + 4 <= p.N) {
+          uint2 prev = make_uint2(0u, 0u);
+          if (read_c) prev = *reinterpret_cast<const uint2*>(dst);
+          const float c0 = read_c ? half_bits_to_float(prev.x & 0xFFFFu) : 0.0f;
+          const float c1 = read_c ? half_bits_to_float(prev.x >> 16) : 0.0f;
+          const float c2 = read_c ? half_bits_to_float(prev.y & 0xFFFFu) : 0.0f;
+          const float c3 = read_c ? half_bits_to_float(prev.y >> 16) : 0.0f;
+          *reinterpret_cast<uint2*>(dst) =
+              make_uint2(pack_half2(fmaf(p.alpha, s4[0], p.beta * c0), fmaf(p.alpha, s4[1], p.beta * c1)),
+                         pack_half2(fmaf(p.alpha, s4[2], p.beta * c2), fmaf(p.alpha, s4[3], p.beta * c3)));
+        } else {
+  #pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (col + e < p.N) {
+              const float prev = read_c ? __half2float(dst[e]) : 0.0f;
+              dst[e] = __float2half_rn(fmaf(p.alpha, s4[e], p.beta * prev));
+            }
+          }
+        }
+      }
+      cluster_sync_all();  // peers may still be reading this CTA's partial
+    } else {
+      __syncthreads();
+    }
   }
   if (warp == 1) {
     tc_fence_after();

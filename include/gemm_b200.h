@@ -61,7 +61,9 @@ GEMM_API void gemm_launcher_stream(const gemm_half_t* A, const gemm_half_t* B, g
  * output tile (tcgen05.mma.cta_group::1); 2 = a 2-CTA cluster per 256 x 256
  * output tile (tcgen05.mma.cta_group::2); 3 = a 2-CTA cluster per 512 x 256
  * output tile (two 128-row A slabs per CTA); 4 = a 2-CTA cluster per 256 x 512
- * output tile (two B tiles per CTA sharing A through the A collector).
+ * output tile (two B tiles per CTA sharing A through the A collector); 5 = one
+ * CTA per 128 x 256 tile with the K range split over a cluster of 2-8 CTAs
+ * (partials added through distributed shared memory).
  * Returns 0, or -1 if the forced path cannot serve the shape. */
 GEMM_API int gemm_launcher_ex(const gemm_half_t* A, const gemm_half_t* B, gemm_half_t* C, int M, int N,
                      int K, float alpha, float beta, cudaStream_t stream, int path, int tile_n);

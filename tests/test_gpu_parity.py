@@ -60,6 +60,23 @@ def test_tc_path(lib, cuda, shape, tile_n):
     _go(lib, cuda, m, n, k, 0.75, 0.5, dist="normal", path=PATH_TC, tile_n=tile_n, seed=m + n + k)
 
 
+# Cluster split-K on 128 x 256 tiles (tile code 5): ragged M, N and K, the
+# automatic choice at 1024^3, a misaligned C (the reduction's scalar stores).
+SPLIT_K_SHAPES = [(1024, 1024, 1024), (129, 257, 650), (300, 1000, 4104), (1000, 520, 8192),
+                  (64, 4096, 4096), (513, 264, 200)]
+
+
+@pytest.mark.parametrize("shape", SPLIT_K_SHAPES, ids=str)
+@pytest.mark.parametrize("beta", [0.0, -0.5])
+def test_split_k_cluster(lib, cuda, shape, beta):
+    m, n, k = shape
+    _go(lib, cuda, m, n, k, 0.75, beta, dist="normal", path=PATH_TC, tile_n=5, seed=m + 7 * k)
+
+
+def test_split_k_misaligned_c(lib, cuda):
+    _go(lib, cuda, 700, 900, 3000, 0.75, 0.25, path=PATH_TC, tile_n=5, offsets=(0, 0, 1), seed=3)
+
+
 @pytest.mark.parametrize("group", [1, 3, 64, -1, -3, -64])
 @pytest.mark.parametrize("tile_n", [128, 4], ids=["128x128", "pair256x512"])
 def test_tc_raster_orders(lib, cuda, monkeypatch, group, tile_n):
@@ -218,10 +235,11 @@ def test_dispatch_choices(lib, cuda):
     assert names[(3, 5000, 4097)].startswith("rows_gemv_kernel<4")
     run(lib, cuda, 8, 6144, 4096, fn="launcher")
     assert gemm_b200.last_kernel().startswith("skinny_tc_kernel<16>")
-    # 64 < M <= 256: the split-K small-M kernel for modest N and long K, dense otherwise
-    run(lib, cuda, 128, 4096, 4096, fn="launcher")
+    # 64 < M <= 128 with K >= 3N: the small-M kernel; otherwise the dense path, whose
+    # 128 x 256 tiles split K over a cluster when they are too few to fill the GPU
+    run(lib, cuda, 96, 4096, 14336, fn="launcher")
     assert gemm_b200.last_kernel().startswith("skinny_tc_kernel<128>")
+    run(lib, cuda, 128, 4096, 4096, fn="launcher")
+    assert gemm_b200.last_kernel().startswith("tc_gemm_kernel<128x256>")
     run(lib, cuda, 200, 4096, 8192, fn="launcher")
-    assert gemm_b200.last_kernel().startswith("skinny_tc_kernel<256>")
-    run(lib, cuda, 128, 14336, 4096, fn="launcher")
     assert gemm_b200.last_kernel().startswith("tc_gemm_kernel")
