@@ -113,6 +113,11 @@ int env_int(const char* name) {
   return v ? std::atoi(v) : 0;
 }
 
+int env_int_default(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return v && *v ? std::atoi(v) : dflt;
+}
+
 template <int BN, bool PAIR, int SLABS, bool SLAB_N = false>
 void configure_tc() {
   cudaFuncSetAttribute(tc_gemm_kernel<BN, PAIR, false, SLABS, SLAB_N>,
@@ -311,6 +316,10 @@ constexpr int kTilePairN = 4;
 // cluster of 2, 4 or 8 CTAs (a request for tests; the automatic choice applies
 // split_k_plan()).
 constexpr int kTileSplitK = 5;
+// A split-K CTA parks its FP32 partial (128 rows x (256 + 4) floats) in the
+// stage ring once its UMMAs are done.
+static_assert(TcCfg<256, false>::kStages * TcCfg<256, false>::kStageBytes >= 128 * 260 * 4,
+              "split-K partial must fit the stage ring");
 
 // Split-K for small and mid-size problems: when 128 x 256 tiles are too few to
 // fill the GPU, the K range of each tile is split over a cluster (DSMEM
@@ -378,6 +387,12 @@ int raster_group(int tiles_m, int tiles_n) {
   return std::max(1, std::min(tiles_m, g > 0 ? g : 16));
 }
 
+// Programmatic dependent launch for the tcgen05 kernels: a kernel may start
+// its set-up (barrier init, TMEM allocation, descriptor prefetch) while the
+// previous kernel in the stream finishes; it waits for that kernel before its
+// first global-memory access (griddepcontrol.wait). GEMM_PDL=0 turns it off.
+bool pdl_enabled() { return env_int_default("GEMM_PDL", 1) != 0; }
+
 template <int BN, bool PAIR, bool BKM, int SLABS, bool SLAB_N = false>
 void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                   const TcParams& p, const DeviceInfo& d, cudaStream_t s, int M, int N, int K,
@@ -394,49 +409,42 @@ void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   const int idx =
       PAIR ? (SLAB_N ? 5 : (SLABS == 2 ? 4 : 3)) : (BN == 64 ? 0 : (BN == 128 ? 1 : 2));
   const char* name = names[BKM ? 1 : 0][idx];
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
   if constexpr (PAIR) {
     const int cap = SLAB_N ? d.pairn_clusters : (SLABS == 2 ? d.pair2_clusters : d.pair_clusters);
     const int clusters =
         std::min(tiles, max_sms > 0 ? std::min(cap, std::max(1, max_sms / 2)) : cap);
-    cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
-    cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
-    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    log_launch(name, M, N, K, cfg.gridDim, cfg.blockDim);
-    record_error(
-        cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, true, BKM, SLABS, SLAB_N>, ta, tb, tc, p));
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 2;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
   } else if (p.ksplit > 1) {
     // split-K: one CTA per (tile, K part), the parts of a tile in one cluster
-    cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(tiles, p.ksplit, 1);
-    cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
-    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = p.ksplit;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    log_launch(name, M, N, K, cfg.gridDim, cfg.blockDim);
-    record_error(
-        cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, false, BKM, SLABS, SLAB_N>, ta, tb, tc, p));
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = p.ksplit;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
   } else {
-    const int grid = std::min(tiles, max_sms > 0 ? std::min(d.sms, max_sms) : d.sms);
-    log_launch(name, M, N, K, dim3(grid), dim3(Cfg::kThreads));
-    tc_gemm_kernel<BN, false, BKM, SLABS, SLAB_N>
-        <<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(ta, tb, tc, p);
-    record_error(cudaGetLastError());
+    cfg.gridDim = dim3(std::min(tiles, max_sms > 0 ? std::min(d.sms, max_sms) : d.sms), 1, 1);
   }
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  log_launch(name, M, N, K, cfg.gridDim, cfg.blockDim);
+  record_error(cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, PAIR, BKM, SLABS, SLAB_N>, ta, tb, tc, p));
 }
 
 // Encode the tensor maps and launch the tcgen05 kernel for `tile` on operands

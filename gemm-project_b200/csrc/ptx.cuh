@@ -289,13 +289,14 @@ __device__ __forceinline__ void umma_commit_local(uint32_t bar) {
 }
 
 // Commit to the barrier at this shared offset in every CTA that waits on it:
-// this CTA, plus the odd CTA of the pair (one commit each, no multicast form).
+// this CTA, plus the odd CTA of the pair, cluster rank `peer_rank` (one commit
+// each, no multicast form).
 template <bool PAIR>
-__device__ __forceinline__ void umma_commit_to(uint32_t local_bar) {
+__device__ __forceinline__ void umma_commit_to(uint32_t local_bar, uint32_t peer_rank = 1) {
   umma_commit_local<PAIR>(local_bar);
   if constexpr (PAIR) {
     uint32_t peer;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, 1;" : "=r"(peer) : "r"(local_bar));
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer) : "r"(local_bar), "r"(peer_rank));
     umma_commit_local<PAIR>(peer);
   }
 }
@@ -388,6 +389,20 @@ __device__ __forceinline__ void cluster_arrive_release() {
 
 __device__ __forceinline__ void cluster_wait_acquire() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Programmatic dependent launch. launch_dependents: this CTA no longer holds
+// back the launch of the next kernel in the stream (if that kernel was
+// launched as a programmatic dependent, its CTAs may start on free SMs once
+// every CTA of this grid has executed this or exited). wait: block until the
+// grids this one depends on have completed and their memory is visible; a
+// kernel launched as a programmatic dependent executes it before its first
+// global-memory access. Both are no-ops without a programmatic dependency.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // Full cluster barrier (all threads of all CTAs), with release/acquire ordering.

@@ -115,6 +115,9 @@ struct TcCfg {
   // kRegsCtl per thread, the two epilogue warpgroups rise to kRegsEpi. The
   // shares must fit in what the block is launched with (kThreads x the
   // kernel's register count); the launcher checks this before using the tile.
+  // Split-K (the K range of a tile over a cluster, FP32 partials added through
+  // DSMEM) exists for the single-CTA 128 x 256 tile.
+  static constexpr bool kSplitK = BN_ == 256 && !PAIR_ && SLABS_ == 1 && !SLAB_N_;
   static constexpr int kRegsCtl = 48;
   static constexpr int kRegsEpi = 224;
   static constexpr int kRegSplitTotal = 128 * kRegsCtl + 32 * kEpiWarps * kRegsEpi;
@@ -243,6 +246,81 @@ __device__ __forceinline__ void epilogue_chunk_lsu(const TcParams& p, float* til
   __syncwarp();
 }
 
+// Split-K reduction of one CTA's share of a tile: rows [q * 128 / KS, (q + 1) *
+// 128 / KS) of the 128-row partials, summed over the KS partials (partial k in
+// the shared memory of cluster rank k at the same offset as `part` here, row
+// pitch BN + 4 floats), then alpha * sum + beta * C rounded to half and stored
+// to C (tile origin row0, col0). Each thread keeps 16 DSMEM float4 loads in
+// flight: issued one at a time they are latency-bound.
+template <int KS, int BN>
+__device__ __forceinline__ void splitk_reduce(const TcParams& p, uint32_t part, int q, int row0,
+                                              int col0) {
+  constexpr int kRows = 128 / KS;
+  constexpr int kCols4 = BN / 4;
+  constexpr int kItems = kRows * kCols4;
+  constexpr int kU = 16 / KS;  // items per thread per pass
+  const bool read_c = p.beta != 0.0f;
+  uint32_t base[KS];
+#pragma unroll
+  for (int k = 0; k < KS; ++k) base[k] = mapa_shared(part, static_cast<uint32_t>(k));
+  for (int i0 = threadIdx.x; i0 < kItems; i0 += kU * blockDim.x) {
+    float4 v[kU][KS];
+    uint2 prev[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int i = i0 + u * blockDim.x;
+      prev[u] = make_uint2(0u, 0u);
+      if (i < kItems) {
+        const int r = q * kRows + i / kCols4;
+        const int c4 = i % kCols4;
+        const uint32_t off = static_cast<uint32_t>((r * (BN + 4) + 4 * c4) * 4);
+#pragma unroll
+        for (int k = 0; k < KS; ++k) v[u][k] = ld_shared_cluster_v4(base[k] + off);
+        const int row = row0 + r;
+        const int col = col0 + 4 * c4;
+        if (read_c && row < p.M && p.c_vec_ok && col + 4 <= p.N)
+          prev[u] = *reinterpret_cast<const uint2*>(p.C + static_cast<size_t>(row) * p.ldc + col);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i >= kItems) break;
+      const int r = q * kRows + i / kCols4;
+      const int row = row0 + r;
+      const int col = col0 + 4 * (i % kCols4);
+      if (row >= p.M) continue;
+      float4 sum = v[u][0];
+#pragma unroll
+      for (int k = 1; k < KS; ++k) {
+        sum.x += v[u][k].x;
+        sum.y += v[u][k].y;
+        sum.z += v[u][k].z;
+        sum.w += v[u][k].w;
+      }
+      half* dst = p.C + static_cast<size_t>(row) * p.ldc + col;
+      const float s4[4] = {sum.x, sum.y, sum.z, sum.w};
+      if (p.c_vec_ok && col + 4 <= p.N) {
+        const float c0 = read_c ? half_bits_to_float(prev[u].x & 0xFFFFu) : 0.0f;
+        const float c1 = read_c ? half_bits_to_float(prev[u].x >> 16) : 0.0f;
+        const float c2 = read_c ? half_bits_to_float(prev[u].y & 0xFFFFu) : 0.0f;
+        const float c3 = read_c ? half_bits_to_float(prev[u].y >> 16) : 0.0f;
+        *reinterpret_cast<uint2*>(dst) =
+            make_uint2(pack_half2(fmaf(p.alpha, s4[0], p.beta * c0), fmaf(p.alpha, s4[1], p.beta * c1)),
+                       pack_half2(fmaf(p.alpha, s4[2], p.beta * c2), fmaf(p.alpha, s4[3], p.beta * c3)));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (col + e < p.N) {
+            const float pc = read_c ? __half2float(dst[e]) : 0.0f;
+            dst[e] = __float2half_rn(fmaf(p.alpha, s4[e], p.beta * pc));
+          }
+        }
+      }
+    }
+  }
+}
+
 template <int BN, bool PAIR, bool BKM, int SLABS, bool SLAB_N>
 __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -283,9 +361,17 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // position in the CTA pair
+  // A CTA pair is two cluster ranks that differ in bit 0; with split-K a
+  // cluster holds several pairs (one per K part). `rank` is the position in
+  // the pair, `pbase` the pair's even cluster rank.
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+  const uint32_t rank = crank & 1u;
+  const uint32_t pbase = crank & ~1u;
   const bool leader = rank == 0;
 
+  // The next kernel in the stream may start its set-up on free SMs now (it
+  // waits for this grid before touching global memory).
+  griddep_launch_dependents();
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(full_bar(s), 1);
@@ -307,11 +393,6 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
     tma_prefetch_desc(&tmap_b);
     if (p.c_tma) tma_prefetch_desc(&tmap_c);
   }
-  if constexpr (PAIR) {
-    cluster_sync_all();  // peer barriers initialised before any remote arrival
-  } else {
-    __syncthreads();
-  }
   if (warp == 1) {
     if constexpr (PAIR) {
       tmem_alloc_pair(smem_u32(tmem_slot), Cfg::kTmemCols);
@@ -321,6 +402,8 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
       tmem_relinquish();
     }
   }
+  // One barrier publishes both: the (peer) mbarriers are initialised before
+  // any remote arrival, and the TMEM address is in tmem_slot.
   tc_fence_before();
   if constexpr (PAIR) {
     cluster_sync_all();
@@ -328,6 +411,9 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
     __syncthreads();
   }
   tc_fence_after();
+  // Launched as a programmatic dependent: A, B and C may still be written by
+  // the previous kernel until it completes.
+  griddep_wait();
   const uint32_t tmem_base = *tmem_slot;
 
   const int num_tiles = p.tiles_m * p.tiles_n;
@@ -359,7 +445,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
               break;
             }
             if (leader) mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes * (PAIR ? 2 : 1));
-            const uint32_t fb = PAIR ? mapa_shared(full_bar(stage), 0) : full_bar(stage);
+            const uint32_t fb = PAIR ? mapa_shared(full_bar(stage), pbase) : full_bar(stage);
             tma_load_2d<PAIR>(sA0 + stage * Cfg::kABytes, &tmap_a, fb, kb * Cfg::BK, m0);
   #pragma unroll
             for (int h = 0; h < Cfg::kSlabsN; ++h) {
@@ -382,10 +468,23 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
         }
       }
     } else if (warp == 1) {
-      if (leader) {
+      // The 256x512 tile runs this loop on the whole warp (descriptors and
+      // TMEM addresses warp-uniform, one elected lane issuing each tcgen05
+      // instruction); the other tiles run it on one thread, which issues
+      // everything without per-instruction election and re-convergence
+      // (measured on B200: K steps of the smaller tiles about 20% shorter,
+      // the 256x512 tile about 6% slower).
+      constexpr bool kOneThread = !SLAB_N;
+      auto issuer = [&]() { return kOneThread ? true : elect_one(); };
+      auto converge = [&]() {
+        if constexpr (!kOneThread) __syncwarp();
+      };
+      auto wait = [&](uint32_t bar, uint32_t parity, volatile int* flag) {
+        return kOneThread ? mbar_wait(bar, parity, p.timeout_ns, flag, p.err, kErrTimeoutMma)
+                          : mbar_wait_warp(bar, parity, p.timeout_ns, flag, p.err, kErrTimeoutMma);
+      };
+      if (leader && (!kOneThread || lane == 0)) {
         // ---------------- UMMA issuer (even CTA) ----------------
-        // The whole warp runs this loop so that descriptors and TMEM addresses
-        // stay warp-uniform; one elected lane issues each tcgen05 instruction.
         constexpr uint32_t idesc = make_idesc_f16(Cfg::kMmaM, BN, /*a_mn_major=*/false,
                                                   /*b_mn_major=*/!BKM);
         int stage = 0;
@@ -395,8 +494,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
         bool ok = true;
         for (int t = unit; t < num_tiles && ok; t += num_units) {
           for (int kb = kb_lo; kb < kb_hi && ok; ++kb) {
-            if (!mbar_wait_warp(full_bar(stage), phase, p.timeout_ns, abort_flag, p.err,
-                                kErrTimeoutMma)) {
+            if (!wait(full_bar(stage), phase, abort_flag)) {
               ok = false;
               break;
             }
@@ -409,8 +507,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
               if (kb == kb_lo) {
   #pragma unroll
                 for (int sl = 0; sl < SLABS; ++sl)
-                  if (ok && !mbar_wait_warp(tempty_bar(acc, sl), acc_phase ^ 1u, p.timeout_ns,
-                                            abort_flag, p.err, kErrTimeoutMma))
+                  if (ok && !wait(tempty_bar(acc, sl), acc_phase ^ 1u, abort_flag))
                     ok = false;
                 if (!ok) break;
                 tc_fence_after();
@@ -426,26 +523,25 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
                     BKM ? make_smem_desc(b_addr + Cfg::kBSlabBytes + kk * 32, 16, 1024)
                         : make_smem_desc(b_addr + Cfg::kBSlabBytes + kk * 2048, Cfg::kBBoxBytes,
                                          1024);
-                if (elect_one()) {
+                if (issuer()) {
                   umma_f16<PAIR, 1>(d0, adesc, b0, idesc, en);
                   umma_f16<PAIR, 2>(d0 + BN, adesc, b1, idesc, en);
                 }
-                __syncwarp();
+                converge();
               }
               if (kb == kb_hi - 1) {
-                if (elect_one()) {
+                if (issuer()) {
   #pragma unroll
-                  for (int sl = 0; sl < SLABS; ++sl) umma_commit_to<PAIR>(tfull_bar(acc, sl));
+                  for (int sl = 0; sl < SLABS; ++sl) umma_commit_to<PAIR>(tfull_bar(acc, sl), pbase | 1u);
                 }
-                __syncwarp();
+                converge();
               }
             } else {
   #pragma unroll
               for (int sl = 0; sl < SLABS; ++sl) {
                 if (kb == kb_lo) {
                   // this slab's accumulator must have been drained by the epilogue
-                  if (!mbar_wait_warp(tempty_bar(acc, sl), acc_phase ^ 1u, p.timeout_ns, abort_flag,
-                                      p.err, kErrTimeoutMma)) {
+                  if (!wait(tempty_bar(acc, sl), acc_phase ^ 1u, abort_flag)) {
                     ok = false;
                     break;
                   }
@@ -465,19 +561,19 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
                   const uint64_t bdesc =
                       BKM ? make_smem_desc(b_addr + kk * 32, 16, 1024)
                           : make_smem_desc(b_addr + kk * 2048, Cfg::kBBoxBytes, 1024);
-                  if (elect_one())
+                  if (issuer())
                     umma_f16<PAIR>(d_tmem, adesc, bdesc, idesc, (kb != kb_lo || kk != 0) ? 1u : 0u);
-                  __syncwarp();
+                  converge();
                 }
                 if (kb == kb_hi - 1) {
-                  if (elect_one()) umma_commit_to<PAIR>(tfull_bar(acc, sl));
-                  __syncwarp();
+                  if (issuer()) umma_commit_to<PAIR>(tfull_bar(acc, sl), pbase | 1u);
+                  converge();
                 }
               }
             }
             if (!ok) break;
-            if (elect_one()) umma_commit_to<PAIR>(empty_bar(stage));
-            __syncwarp();
+            if (issuer()) umma_commit_to<PAIR>(empty_bar(stage), pbase | 1u);
+            converge();
             if (++stage == kStages) {
               stage = 0;
               phase ^= 1u;
@@ -488,11 +584,11 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
             acc_phase ^= 1u;
           }
         }
-        // Drain: all UMMAs issued by the elected lane complete before TMEM is freed.
-        if (elect_one()) umma_commit_local<PAIR>(final_bar);
-        __syncwarp();
+        // Drain: all UMMAs issued here complete before TMEM is freed.
+        if (issuer()) umma_commit_local<PAIR>(final_bar);
+        converge();
         volatile int no_abort = 0;
-        mbar_wait_warp(final_bar, 0, p.timeout_ns, &no_abort, p.err, kErrTimeoutMma);
+        wait(final_bar, 0, &no_abort);
       }
     }
   } else {
@@ -556,7 +652,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
           if (leader)
             mbar_arrive(tempty_bar(0, sl));
           else
-            mbar_arrive_remote_signal(mapa_shared(tempty_bar(0, sl), 0));
+            mbar_arrive_remote_signal(mapa_shared(tempty_bar(0, sl), pbase));
         }
         return true;
       };
@@ -639,7 +735,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
           const int col_base = tn * Cfg::kTileN + col_half * Cfg::kEpiCols;
           // Prefetch this slab's first two C boxes while its UMMAs still run
           // (not with split-K, whose cluster reduction reads C itself).
-          if (p.c_tma && read_c && lane == 0 && (PAIR || p.ksplit <= 1)) {
+          if (p.c_tma && read_c && lane == 0 && p.ksplit <= 1) {
             bulk_wait_read<0>();  // earlier TMA stores have finished reading both buffers
             issue_c_load(ctr, col_base, row_base);
             if (kChunks > 1) issue_c_load(ctr + 1, col_base + Cfg::kEpiChunk, row_base);
@@ -650,7 +746,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
             break;
           }
           tc_fence_after();
-          if (!PAIR && p.ksplit > 1) {
+          if (Cfg::kSplitK && p.ksplit > 1) {
             // Split-K: this CTA's FP32 partial of the tile into the idle stage
             // ring, rows padded by 4 floats (bank-conflict-free float4 rows);
             // the cluster reduction after the role branches writes C.
@@ -686,7 +782,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
           if (lane == 0) {
             // the even CTA's barrier gates the next tile's UMMAs
             if (PAIR && !leader)
-              mbar_arrive_remote_signal(mapa_shared(tempty_bar(acc, sl), 0));
+              mbar_arrive_remote_signal(mapa_shared(tempty_bar(acc, sl), pbase));
             else
               mbar_arrive(tempty_bar(acc, sl));
           }
@@ -757,61 +853,28 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
 
   tc_fence_before();
   __syncwarp();
-  if constexpr (PAIR) {
-    cluster_sync_all();  // no CTA leaves while its peer may still signal it
-  } else {
-    if (p.ksplit > 1) {
-      // Split-K reduction: every CTA of the cluster holds a partial of the same
-      // tile; CTA q adds all partials for its slice of rows through DSMEM and
-      // writes those rows of C (4 columns per thread step, 8-byte stores).
-      cluster_sync_all();  // all partials written and visible
-      const float* part = reinterpret_cast<const float*>(smem);
+  if (Cfg::kSplitK && p.ksplit > 1) {
+    // Split-K reduction: the ksplit CTAs of the cluster each hold an FP32
+    // partial of the same tile; CTA q of them reduces slice q of the rows.
+    cluster_sync_all();  // all partials written and visible
+    if constexpr (Cfg::kSplitK) {
       const int q = static_cast<int>(cluster_ctarank());
-      const int rows = Cfg::BM / p.ksplit;
       int tm, tn;
       tile_coords(unit, p.tiles_m, p.tiles_n, p.group, tm, tn);
-      const bool read_c = p.beta != 0.0f;
-      for (int i = threadIdx.x; i < rows * (BN / 4); i += blockDim.x) {
-        const int r = q * rows + i / (BN / 4);
-        const int c4 = i % (BN / 4);
-        const uint32_t local = smem_u32(part + r * (BN + 4) + 4 * c4);
-        float4 sum = ld_shared_cluster_v4(mapa_shared(local, 0));
-        for (int k = 1; k < p.ksplit; ++k) {
-          const float4 v = ld_shared_cluster_v4(mapa_shared(local, static_cast<uint32_t>(k)));
-          sum.x += v.x;
-          sum.y += v.y;
-          sum.z += v.z;
-          sum.w += v.w;
-        }
-        const int row = tm * Cfg::kTileM + r;
-        const int col = tn * Cfg::kTileN + 4 * c4;
-        if (row >= p.M) continue;
-        half* dst = p.C + static_cast<size_t>(row) * p.ldc + col;
-        const float s4[4] = {sum.x, sum.y, sum.z, sum.w};
-        if (p.c_vec_ok && col + 4 <= p.N) {
-          uint2 prev = make_uint2(0u, 0u);
-          if (read_c) prev = *reinterpret_cast<const uint2*>(dst);
-          const float c0 = read_c ? half_bits_to_float(prev.x & 0xFFFFu) : 0.0f;
-          const float c1 = read_c ? half_bits_to_float(prev.x >> 16) : 0.0f;
-          const float c2 = read_c ? half_bits_to_float(prev.y & 0xFFFFu) : 0.0f;
-          const float c3 = read_c ? half_bits_to_float(prev.y >> 16) : 0.0f;
-          *reinterpret_cast<uint2*>(dst) =
-              make_uint2(pack_half2(fmaf(p.alpha, s4[0], p.beta * c0), fmaf(p.alpha, s4[1], p.beta * c1)),
-                         pack_half2(fmaf(p.alpha, s4[2], p.beta * c2), fmaf(p.alpha, s4[3], p.beta * c3)));
-        } else {
-  #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            if (col + e < p.N) {
-              const float prev = read_c ? __half2float(dst[e]) : 0.0f;
-              dst[e] = __float2half_rn(fmaf(p.alpha, s4[e], p.beta * prev));
-            }
-          }
-        }
+      const int row0 = tm * Cfg::kTileM;
+      const int col0 = tn * Cfg::kTileN;
+      const uint32_t part = smem_u32(smem);
+      switch (p.ksplit) {
+        case 2: splitk_reduce<2, BN>(p, part, q, row0, col0); break;
+        case 4: splitk_reduce<4, BN>(p, part, q, row0, col0); break;
+        default: splitk_reduce<8, BN>(p, part, q, row0, col0); break;
       }
-      cluster_sync_all();  // peers may still be reading this CTA's partial
-    } else {
-      __syncthreads();
     }
+    cluster_sync_all();  // peers may still be reading this CTA's partial
+  } else if constexpr (PAIR) {
+    cluster_sync_all();  // no CTA leaves while its peer may still signal it
+  } else {
+    __syncthreads();
   }
   if (warp == 1) {
     tc_fence_after();
