@@ -81,12 +81,20 @@ struct TcCfg {
   static constexpr int kBCols = kPair ? BN / 2 : BN;    // B columns of one N slab in one CTA
   static constexpr int BK = 64;                         // one 128-byte swizzle row of FP16
   static constexpr int kSlabBytes = BM * BK * 2;        // 16 KiB: one A slab
-  static constexpr int kABytes = kCtaRows * BK * 2;
+  // K blocks (64 wide) per pipeline stage. The producer/MMA handshake of a
+  // stage costs about as much as six UMMA issues (measured on B200: ~360
+  // cycles per stage with no loads and no UMMAs), so the 128x64, 128x128 and
+  // 256x256 pair tiles carry two K blocks per stage: one handshake per eight
+  // UMMAs.
+  static constexpr int kKSub = ((!PAIR_ && BN_ <= 128) || (PAIR_ && SLABS_ == 1)) ? 2 : 1;
+  static constexpr int kABlk = kCtaRows * BK * 2;       // A of one K block
+  static constexpr int kABytes = kABlk * kKSub;
   // B boxes: N-major B as 64(N) x 64(K) boxes of 8 KiB; K-major B as one box
   // of kBCols rows x 64 K.
   static constexpr int kBBoxBytes = BKM_ ? kBCols * BK * 2 : 64 * BK * 2;
   static constexpr int kBSlabBytes = kBCols * BK * 2;   // B tile of one N slab
-  static constexpr int kBBytes = kBSlabBytes * kSlabsN;
+  static constexpr int kBBlk = kBSlabBytes * kSlabsN;  // B of one K block
+  static constexpr int kBBytes = kBBlk * kKSub;
   static constexpr int kStageBytes = kABytes + kBBytes;
   // Epilogue: two warps per TMEM lane quadrant, each owning half of the tile's
   // columns; C moves through 32 x 32 boxes (64-byte rows, 64B swizzle),
@@ -438,26 +446,34 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
           tile_coords(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
           const int m0 = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kCtaRows;
           const int n0 = tn * Cfg::kTileN + static_cast<int>(rank) * Cfg::kBCols;
-          for (int kb = kb_lo; kb < kb_hi; ++kb) {
+          for (int kb = kb_lo; kb < kb_hi; kb += Cfg::kKSub) {
+            const int nsub = min(Cfg::kKSub, kb_hi - kb);  // K blocks in this stage
             if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag, p.err,
                            kErrTimeoutProducer)) {
               ok = false;
               break;
             }
-            if (leader) mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes * (PAIR ? 2 : 1));
+            if (leader)
+              mbar_arrive_expect_tx(full_bar(stage),
+                                    nsub * (Cfg::kABlk + Cfg::kBBlk) * (PAIR ? 2 : 1));
             const uint32_t fb = PAIR ? mapa_shared(full_bar(stage), pbase) : full_bar(stage);
-            tma_load_2d<PAIR>(sA0 + stage * Cfg::kABytes, &tmap_a, fb, kb * Cfg::BK, m0);
   #pragma unroll
-            for (int h = 0; h < Cfg::kSlabsN; ++h) {
-              const uint32_t sb = sB0 + stage * Cfg::kBBytes + h * Cfg::kBSlabBytes;
-              const int nh = n0 + h * BN;
-              if constexpr (BKM) {
-                tma_load_2d<PAIR>(sb, &tmap_b, fb, kb * Cfg::BK, nh);
-              } else {
+            for (int q = 0; q < Cfg::kKSub; ++q) {
+              if (q >= nsub) break;
+              const int kx = (kb + q) * Cfg::BK;
+              tma_load_2d<PAIR>(sA0 + stage * Cfg::kABytes + q * Cfg::kABlk, &tmap_a, fb, kx, m0);
   #pragma unroll
-                for (int j = 0; j < Cfg::kBCols / 64; ++j)
-                  tma_load_2d<PAIR>(sb + j * Cfg::kBBoxBytes, &tmap_b, fb, nh + 64 * j,
-                                    kb * Cfg::BK);
+              for (int h = 0; h < Cfg::kSlabsN; ++h) {
+                const uint32_t sb =
+                    sB0 + stage * Cfg::kBBytes + q * Cfg::kBBlk + h * Cfg::kBSlabBytes;
+                const int nh = n0 + h * BN;
+                if constexpr (BKM) {
+                  tma_load_2d<PAIR>(sb, &tmap_b, fb, kx, nh);
+                } else {
+  #pragma unroll
+                  for (int j = 0; j < Cfg::kBCols / 64; ++j)
+                    tma_load_2d<PAIR>(sb + j * Cfg::kBBoxBytes, &tmap_b, fb, nh + 64 * j, kx);
+                }
               }
             }
             if (++stage == kStages) {
@@ -493,7 +509,9 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
         uint32_t acc_phase = 0;
         bool ok = true;
         for (int t = unit; t < num_tiles && ok; t += num_units) {
-          for (int kb = kb_lo; kb < kb_hi && ok; ++kb) {
+          for (int kb = kb_lo; kb < kb_hi && ok; kb += Cfg::kKSub) {
+            const int nsub = min(Cfg::kKSub, kb_hi - kb);  // K blocks in this stage
+            const bool last = kb + nsub == kb_hi;
             if (!wait(full_bar(stage), phase, abort_flag)) {
               ok = false;
               break;
@@ -529,7 +547,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
                 }
                 converge();
               }
-              if (kb == kb_hi - 1) {
+              if (last) {
                 if (issuer()) {
   #pragma unroll
                   for (int sl = 0; sl < SLABS; ++sl) umma_commit_to<PAIR>(tfull_bar(acc, sl), pbase | 1u);
@@ -550,22 +568,28 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
                 const uint32_t d_tmem =
                     tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols + sl * BN);
   #pragma unroll
-                for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
-                  // A: K-major, 128B swizzle; advance 16 K-elements = 32 bytes
-                  // inside the swizzle row. SBO = 8 rows * 128 B.
-                  const uint64_t adesc =
-                      make_smem_desc(a_addr + sl * Cfg::kSlabBytes + kk * 32, 16, 1024);
-                  // B, N-major: 128B swizzle; 16 K-rows = two 8-row groups of
-                  // 1024 B. LBO = distance between 64-column boxes, SBO = 8 K-rows.
-                  // B, K-major: laid out like A (rows of 64 K, 32 bytes per K step).
-                  const uint64_t bdesc =
-                      BKM ? make_smem_desc(b_addr + kk * 32, 16, 1024)
-                          : make_smem_desc(b_addr + kk * 2048, Cfg::kBBoxBytes, 1024);
-                  if (issuer())
-                    umma_f16<PAIR>(d_tmem, adesc, bdesc, idesc, (kb != kb_lo || kk != 0) ? 1u : 0u);
-                  converge();
+                for (int q = 0; q < Cfg::kKSub; ++q) {
+                  if (q >= nsub) break;
+                  const uint32_t aq = a_addr + q * Cfg::kABlk + sl * Cfg::kSlabBytes;
+                  const uint32_t bq = b_addr + q * Cfg::kBBlk;
+  #pragma unroll
+                  for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
+                    // A: K-major, 128B swizzle; advance 16 K-elements = 32 bytes
+                    // inside the swizzle row. SBO = 8 rows * 128 B.
+                    const uint64_t adesc = make_smem_desc(aq + kk * 32, 16, 1024);
+                    // B, N-major: 128B swizzle; 16 K-rows = two 8-row groups of
+                    // 1024 B. LBO = distance between 64-column boxes, SBO = 8
+                    // K-rows. B, K-major: laid out like A (rows of 64 K, 32 bytes
+                    // per K step).
+                    const uint64_t bdesc =
+                        BKM ? make_smem_desc(bq + kk * 32, 16, 1024)
+                            : make_smem_desc(bq + kk * 2048, Cfg::kBBoxBytes, 1024);
+                    const uint32_t en = (kb + q != kb_lo || kk != 0) ? 1u : 0u;
+                    if (issuer()) umma_f16<PAIR>(d_tmem, adesc, bdesc, idesc, en);
+                    converge();
+                  }
                 }
-                if (kb == kb_hi - 1) {
+                if (last) {
                   if (issuer()) umma_commit_to<PAIR>(tfull_bar(acc, sl), pbase | 1u);
                   converge();
                 }
