@@ -190,18 +190,21 @@ DeviceInfo& device_info() {
                            ? pair_capacity<2, true>(d.sms)
                            : 0;
     {
-      cudaFuncSetAttribute(rows_tma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmemBytes);
-      cudaFuncSetAttribute(rows_tma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmemBytes);
-      cudaFuncSetAttribute(rows_tma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmemBytes);
-      cudaFuncSetAttribute(rows_tma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmemBytes);
-      cudaFuncSetAttribute(col_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmemBytes);
-      int per_sm = 0;
+      cudaFuncSetAttribute(rows_tma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
+      cudaFuncSetAttribute(rows_tma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
+      cudaFuncSetAttribute(rows_tma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
+      cudaFuncSetAttribute(rows_tma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
+      cudaFuncSetAttribute(col_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kColSmemBytes);
+      // Co-resident CTAs of both streaming kernels (the smaller of the two).
+      int per_sm = 0, per_sm_col = 0;
       if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows_tma_kernel<8>, kStreamThreads,
-                                                        kStreamSmemBytes) != cudaSuccess) {
+                                                        kRowsSmemBytes) != cudaSuccess ||
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_col, col_tma_kernel, kStreamThreads,
+                                                        kColSmemBytes) != cudaSuccess) {
         cudaGetLastError();
-        per_sm = 0;
+        per_sm = per_sm_col = 0;
       }
-      d.stream_slots = per_sm * d.sms;
+      d.stream_slots = std::min(per_sm, per_sm_col) * d.sms;
     }
     {
       cudaFuncSetAttribute(skinny_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -728,7 +731,7 @@ void launch_rows_tma_mr(const CUtensorMap& ta, const CUtensorMap& tb, const Stre
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(strips, p.ksplit, 1);
   cfg.blockDim = dim3(kStreamThreads, 1, 1);
-  cfg.dynamicSmemBytes = kStreamSmemBytes;
+  cfg.dynamicSmemBytes = kRowsSmemBytes;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -746,9 +749,9 @@ int launch_rows_tma(const half* A, const half* B, half* C, int M, int N, int K, 
                     float beta, cudaStream_t s, const DeviceInfo& d) {
   const int mr = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
   CUtensorMap ta, tb;
-  if (!(make_tmap(&tb, B, N, K, static_cast<uint64_t>(N) * 2, kStreamCols, kStreamRows,
+  if (!(make_tmap(&tb, B, N, K, static_cast<uint64_t>(N) * 2, kStreamCols, kRowsK,
                   CU_TENSOR_MAP_SWIZZLE_NONE) &&
-        make_tmap(&ta, A, K, M, static_cast<uint64_t>(K) * 2, kStreamRows, mr,
+        make_tmap(&ta, A, K, M, static_cast<uint64_t>(K) * 2, kRowsK, mr,
                   CU_TENSOR_MAP_SWIZZLE_NONE))) {
     record_error(cudaErrorInvalidValue);
     return -1;
@@ -764,7 +767,7 @@ int launch_rows_tma(const half* A, const half* B, half* C, int M, int N, int K, 
   p.alpha = alpha;
   p.beta = beta;
   p.ksplit = ksplit;
-  p.kchunk = ceil_div(ceil_div(K, ksplit), kStreamRows) * kStreamRows;
+  p.kchunk = ceil_div(ceil_div(K, ksplit), kRowsK) * kRowsK;
   p.timeout_ns = wait_timeout_ns();
   p.err = d.err;
   switch (mr) {
@@ -779,14 +782,14 @@ int launch_rows_tma(const half* A, const half* B, half* C, int M, int N, int K, 
 int launch_col_tma(const half* A, const half* B, half* C, int M, int K, float alpha, float beta,
                    cudaStream_t s, const DeviceInfo& d) {
   CUtensorMap ta, tb;
-  if (!(make_tmap(&ta, A, K, M, static_cast<uint64_t>(K) * 2, kStreamCols, kStreamRows,
+  if (!(make_tmap(&ta, A, K, M, static_cast<uint64_t>(K) * 2, kStreamCols, kColRows,
                   CU_TENSOR_MAP_SWIZZLE_NONE) &&
         make_tmap(&tb, B, K, 1, static_cast<uint64_t>(K) * 2, kStreamCols, 1,
                   CU_TENSOR_MAP_SWIZZLE_NONE))) {
     record_error(cudaErrorInvalidValue);
     return -1;
   }
-  const int total_blocks = ceil_div(M, kStreamRows);
+  const int total_blocks = ceil_div(M, kColRows);
   const int per_cta = ceil_div(total_blocks, d.stream_slots);
   const int grid = ceil_div(total_blocks, per_cta);
   StreamParams p{};
@@ -800,7 +803,7 @@ int launch_col_tma(const half* A, const half* B, half* C, int M, int K, float al
   p.timeout_ns = wait_timeout_ns();
   p.err = d.err;
   log_launch("col_tma_kernel", M, 1, K, dim3(grid), dim3(kStreamThreads));
-  col_tma_kernel<<<grid, kStreamThreads, kStreamSmemBytes, s>>>(ta, tb, p);
+  col_tma_kernel<<<grid, kStreamThreads, kColSmemBytes, s>>>(ta, tb, p);
   record_error(cudaGetLastError());
   return 0;
 }
