@@ -7,9 +7,11 @@
 // and pointer alignment, src/gemm.cu:20-24 and :112-133) but routes to sm_100a
 // kernels:
 //   K <= 0                      -> scale_c_kernel (C = beta*C)
-//   M == 1                      -> rows_tma_kernel<1>    (TMA-fed HBM streaming, cluster split-K)
+//   M == 1 (and M == 2)         -> rows_tma_kernel<MR>   (TMA-fed HBM streaming, cluster split-K)
 //   2 <= M <= 64, TMA-friendly  -> skinny_tc_kernel<NM>  (tcgen05, C^T = B^T A^T, cluster split-K)
 //   64 < M <= 128, K >= 3N, TMA-friendly            -> skinny_tc_kernel<128>
+//   M <= 8 otherwise, N % 8 == 0 -> rows_tma_kernel<MR>  (B from its 16-byte line with a
+//                                   column phase; A direct when not TMA-addressable, M <= 4)
 //   M <= 8 otherwise            -> rows_gemv_kernel<MR>  (per-thread loads, any alignment)
 //   N == 1                      -> col_tma_kernel / col_gemv_kernel
 //   otherwise                   -> tc_gemm_kernel<...>   (tcgen05 + TMA + TMEM tiles)
@@ -194,6 +196,9 @@ DeviceInfo& device_info() {
       cudaFuncSetAttribute(rows_tma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
       cudaFuncSetAttribute(rows_tma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
       cudaFuncSetAttribute(rows_tma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
+      cudaFuncSetAttribute(rows_tma_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
+      cudaFuncSetAttribute(rows_tma_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
+      cudaFuncSetAttribute(rows_tma_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
       cudaFuncSetAttribute(col_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kColSmemBytes);
       // Co-resident CTAs of both streaming kernels (the smaller of the two).
       int per_sm = 0, per_sm_col = 0;
@@ -715,19 +720,27 @@ int launch_col(const half* A, const half* B, half* C, int M, int N, int K, float
 // ---------------------------------------------------------------------------
 // TMA-fed streaming kernels (operands TMA-addressable).
 // ---------------------------------------------------------------------------
+// The TMA streaming kernel for M <= 8 needs B's row pitch to be a multiple of
+// 16 bytes (N % 8 == 0); a misaligned B base is handled by a column phase. A
+// is read through TMA when it is TMA-addressable, otherwise directly (M <= 4).
+bool rows_a_tma(const half* A, int K) { return aligned16(A) && K % 8 == 0; }
+
 bool rows_tma_ok(const half* A, const half* B, int M, int N, int K, const DeviceInfo& d) {
-  return d.stream_slots > 0 && M <= 8 && aligned16(A) && aligned16(B) && K % 8 == 0 && N % 8 == 0;
+  return d.stream_slots > 0 && M <= 8 && N % 8 == 0 &&
+         (reinterpret_cast<uintptr_t>(B) & 1u) == 0 && (rows_a_tma(A, K) || M <= 4);
 }
 
 bool col_tma_ok(const half* A, const half* B, int N, int K, const DeviceInfo& d) {
   return d.stream_slots > 0 && N == 1 && aligned16(A) && aligned16(B) && K % 8 == 0;
 }
 
-template <int MR>
+template <int MR, bool A_TMA>
 void launch_rows_tma_mr(const CUtensorMap& ta, const CUtensorMap& tb, const StreamParams& p,
                         int strips, cudaStream_t s, int M, int N, int K) {
-  static const char* names[4] = {"rows_tma_kernel<1>", "rows_tma_kernel<2>", "rows_tma_kernel<4>",
-                                 "rows_tma_kernel<8>"};
+  static const char* names[2][4] = {
+      {"rows_tma_kernel<1,a-direct>", "rows_tma_kernel<2,a-direct>", "rows_tma_kernel<4,a-direct>",
+       "rows_tma_kernel<8,a-direct>"},
+      {"rows_tma_kernel<1>", "rows_tma_kernel<2>", "rows_tma_kernel<4>", "rows_tma_kernel<8>"}};
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(strips, p.ksplit, 1);
   cfg.blockDim = dim3(kStreamThreads, 1, 1);
@@ -740,27 +753,40 @@ void launch_rows_tma_mr(const CUtensorMap& ta, const CUtensorMap& tb, const Stre
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  log_launch(names[MR == 1 ? 0 : (MR == 2 ? 1 : (MR == 4 ? 2 : 3))], M, N, K, cfg.gridDim,
-             cfg.blockDim);
-  record_error(cudaLaunchKernelEx(&cfg, rows_tma_kernel<MR>, ta, tb, p));
+  log_launch(names[A_TMA ? 1 : 0][MR == 1 ? 0 : (MR == 2 ? 1 : (MR == 4 ? 2 : 3))], M, N, K,
+             cfg.gridDim, cfg.blockDim);
+  record_error(cudaLaunchKernelEx(&cfg, rows_tma_kernel<MR, A_TMA>, ta, tb, p));
 }
 
 int launch_rows_tma(const half* A, const half* B, half* C, int M, int N, int K, float alpha,
                     float beta, cudaStream_t s, const DeviceInfo& d) {
   const int mr = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
-  CUtensorMap ta, tb;
-  if (!(make_tmap(&tb, B, N, K, static_cast<uint64_t>(N) * 2, kStreamCols, kRowsK,
-                  CU_TENSOR_MAP_SWIZZLE_NONE) &&
-        make_tmap(&ta, A, K, M, static_cast<uint64_t>(K) * 2, kRowsK, mr,
-                  CU_TENSOR_MAP_SWIZZLE_NONE))) {
+  const bool a_tma = rows_a_tma(A, K);
+  if (!a_tma && mr > 4) {
     record_error(cudaErrorInvalidValue);
     return -1;
   }
-  const int strips = ceil_div(N, kStreamCols);
+  // B's tensor map starts at the 16-byte line B starts in (inside B's
+  // allocation, which is at least 16-byte aligned); strip s then covers B's
+  // columns [256 s - phase, 256 s - phase + 256).
+  const int phase = static_cast<int>((reinterpret_cast<uintptr_t>(B) / 2) % 8);
+  CUtensorMap ta, tb;
+  std::memset(&ta, 0, sizeof(ta));
+  if (!make_tmap(&tb, B - phase, static_cast<uint64_t>(N) + phase, K, static_cast<uint64_t>(N) * 2,
+                 kStreamCols, kRowsK, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      (a_tma && !make_tmap(&ta, A, K, M, static_cast<uint64_t>(K) * 2, kRowsK, mr,
+                           CU_TENSOR_MAP_SWIZZLE_NONE))) {
+    record_error(cudaErrorInvalidValue);
+    return -1;
+  }
+  const int strips = ceil_div(N + phase, kStreamCols);
   int ksplit = 1;
   while (ksplit < 8 && strips * ksplit * 2 <= d.stream_slots && K / (ksplit * 2) >= 256) ksplit *= 2;
   StreamParams p{};
   p.C = C;
+  p.A = A;
+  p.lda = K;
+  p.phase = phase;
   p.M = M;
   p.N = N;
   p.K = K;
@@ -770,11 +796,19 @@ int launch_rows_tma(const half* A, const half* B, half* C, int M, int N, int K, 
   p.kchunk = ceil_div(ceil_div(K, ksplit), kRowsK) * kRowsK;
   p.timeout_ns = wait_timeout_ns();
   p.err = d.err;
-  switch (mr) {
-    case 1: launch_rows_tma_mr<1>(ta, tb, p, strips, s, M, N, K); break;
-    case 2: launch_rows_tma_mr<2>(ta, tb, p, strips, s, M, N, K); break;
-    case 4: launch_rows_tma_mr<4>(ta, tb, p, strips, s, M, N, K); break;
-    default: launch_rows_tma_mr<8>(ta, tb, p, strips, s, M, N, K); break;
+  if (a_tma) {
+    switch (mr) {
+      case 1: launch_rows_tma_mr<1, true>(ta, tb, p, strips, s, M, N, K); break;
+      case 2: launch_rows_tma_mr<2, true>(ta, tb, p, strips, s, M, N, K); break;
+      case 4: launch_rows_tma_mr<4, true>(ta, tb, p, strips, s, M, N, K); break;
+      default: launch_rows_tma_mr<8, true>(ta, tb, p, strips, s, M, N, K); break;
+    }
+  } else {
+    switch (mr) {
+      case 1: launch_rows_tma_mr<1, false>(ta, tb, p, strips, s, M, N, K); break;
+      case 2: launch_rows_tma_mr<2, false>(ta, tb, p, strips, s, M, N, K); break;
+      default: launch_rows_tma_mr<4, false>(ta, tb, p, strips, s, M, N, K); break;
+    }
   }
   return 0;
 }
@@ -899,8 +933,8 @@ int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float a
       tile_n != kTilePair2 && tile_n != kTilePairN && tile_n != kTileSplitK)
     return -1;
   if (path == 0) {
-    if (M == 1)
-      path = 2;                       // streaming GEMV
+    if (M == 1 || (M == 2 && rows_tma_ok(A, B, M, N, K, d)))
+      path = 2;                       // streaming GEMV (M = 2: faster than the tensor-core kernel)
     else if (N > 1 && dec_ok(A, B, M, N, K, d) && (M <= 64 || small_m_wins(M, N, K)))
       path = 6;                       // small-M tensor-core kernel
     else if (M <= 8)

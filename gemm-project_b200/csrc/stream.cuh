@@ -51,6 +51,9 @@ constexpr int kColSmemBytes = kColStages * kColStageBytes + 256 + 128;
 
 struct StreamParams {
   half* C;
+  const half* A;     // rows kernel without an A tensor map: A read directly (pitch lda)
+  int lda;
+  int phase;         // rows kernel: B's element offset inside its 16-byte line
   int M, N, K;
   float alpha, beta;
   int kchunk;        // rows kernel: K rows per CTA (multiple of kRowsK)
@@ -71,9 +74,15 @@ __device__ __forceinline__ void stream_fma8(float (&acc)[8], float a, uint4 v) {
 }
 
 // grid = (column strips, ksplit); cluster = (1, ksplit, 1).
-// tmap_b: B [K, N], box {256 columns, 64 rows}; tmap_a: A [M, K], box {64, MR}.
-template <int MR>
-__global__ void __launch_bounds__(kStreamThreads)
+// tmap_b: B [K, N + phase] starting `phase` elements before B (the 16-byte line
+// B starts in; the row pitch is a multiple of 16 bytes), box {256 columns, 64
+// rows}: strip s covers B's columns [256 s - phase, 256 s - phase + 256).
+// A_TMA: tmap_a is A [M, K], box {64, MR}, loaded with each stage. Otherwise
+// (A not TMA-addressable: misaligned base or K % 8 != 0) each consumer warp
+// reads its stage's A values from global memory into registers before it
+// waits for the stage, so their latency overlaps the wait for B.
+template <int MR, bool A_TMA = true>
+__global__ void __launch_bounds__(kStreamThreads, 2)  // two CTAs per SM: <= 112 registers
     rows_tma_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, const StreamParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -101,7 +110,7 @@ __global__ void __launch_bounds__(kStreamThreads)
     }
     *abort_flag = 0;
     fence_barrier_init();
-    tma_prefetch_desc(&tmap_a);
+    if (A_TMA) tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
   }
   __syncthreads();
@@ -121,10 +130,10 @@ __global__ void __launch_bounds__(kStreamThreads)
         if (!mbar_wait(empty_bar(s), ph ^ 1u, p.timeout_ns, abort_flag, p.err, kErrTimeoutProducer))
           break;
         const uint32_t st = sbase + s * kRowsStageBytes;
-        mbar_arrive_expect_tx(full_bar(s), kRowsBoxBytes + MR * kRowsK * 2);
+        mbar_arrive_expect_tx(full_bar(s), kRowsBoxBytes + (A_TMA ? MR * kRowsK * 2 : 0));
         const int k = k_begin + i * kRowsK;
         tma_load_2d<false>(st, &tmap_b, full_bar(s), strip * kStreamCols, k);
-        tma_load_2d<false>(st + kRowsBoxBytes, &tmap_a, full_bar(s), k, 0);
+        if (A_TMA) tma_load_2d<false>(st + kRowsBoxBytes, &tmap_a, full_bar(s), k, 0);
         if (++s == kRowsStages) {
           s = 0;
           ph ^= 1u;
@@ -135,16 +144,52 @@ __global__ void __launch_bounds__(kStreamThreads)
     // ---------------- consumers: warp w takes stage rows w, w+8, ..., w+56 ----------------
     int s = 0;
     uint32_t ph = 0;
+    constexpr int kRowsPerWarp = kRowsK / kStreamConsumerWarps;
+    constexpr int kAv = A_TMA ? 1 : kRowsPerWarp;
+    constexpr int kAP = (MR + 1) / 2;  // A values of one K row as half2 pairs (rows 2j, 2j + 1)
+    // Without an A tensor map: A of stage i + 1 is loaded into registers while
+    // stage i is waited for and consumed, so its latency stays off the path.
+    auto load_a = [&](int stage_index, __half2 (&dst)[kAv][kAP]) {
+      const int k0 = k_begin + stage_index * kRowsK + warp;  // this warp's rows: k0 + 8 rr
+#pragma unroll
+      for (int rr = 0; rr < kAv; ++rr) {
+        const int k = k0 + rr * kStreamConsumerWarps;
+#pragma unroll
+        for (int j = 0; j < kAP; ++j) {
+          const bool in0 = 2 * j < p.M && k < k_end, in1 = 2 * j + 1 < p.M && k < k_end;
+          const __half h0 = in0 ? p.A[static_cast<size_t>(2 * j) * p.lda + k] : __float2half(0.0f);
+          const __half h1 =
+              in1 ? p.A[static_cast<size_t>(2 * j + 1) * p.lda + k] : __float2half(0.0f);
+          dst[rr][j] = __halves2half2(h0, h1);
+        }
+      }
+    };
+    auto a_value = [&](const __half2 (&src)[kAv][kAP], int rr, int m) {
+      return __half2float((m & 1) ? __high2half(src[rr][m >> 1]) : __low2half(src[rr][m >> 1]));
+    };
+    __half2 av[kAv][kAP], av_next[kAv][kAP];
+    if constexpr (!A_TMA) load_a(0, av);
     for (int i = 0; i < stages_total; ++i) {
+      if constexpr (!A_TMA) {
+        if (i + 1 < stages_total) load_a(i + 1, av_next);
+      }
       if (!mbar_wait_warp(full_bar(s), ph, p.timeout_ns, abort_flag, p.err, kErrTimeoutMma)) break;
       const uint32_t st = sbase + s * kRowsStageBytes;
       const half* sa = reinterpret_cast<const half*>(smem + s * kRowsStageBytes + kRowsBoxBytes);
 #pragma unroll
-      for (int rr = 0; rr < kRowsK / kStreamConsumerWarps; ++rr) {
+      for (int rr = 0; rr < kRowsPerWarp; ++rr) {
         const int r = warp + rr * kStreamConsumerWarps;
         const uint4 v = ld_shared_v4(st + static_cast<uint32_t>(r * kStreamCols * 2 + lane * 16));
 #pragma unroll
-        for (int m = 0; m < MR; ++m) stream_fma8(acc[m], __half2float(sa[m * kRowsK + r]), v);
+        for (int m = 0; m < MR; ++m)
+          stream_fma8(acc[m],
+                      A_TMA ? __half2float(sa[m * kRowsK + r]) : a_value(av, A_TMA ? 0 : rr, m), v);
+      }
+      if constexpr (!A_TMA) {
+#pragma unroll
+        for (int rr = 0; rr < kAv; ++rr)
+#pragma unroll
+          for (int j = 0; j < kAP; ++j) av[rr][j] = av_next[rr][j];
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_bar(s));
@@ -175,11 +220,11 @@ __global__ void __launch_bounds__(kStreamThreads)
     __syncthreads();
   }
 
-  const int col0 = strip * kStreamCols;
+  const int col0 = strip * kStreamCols - p.phase;
   const bool read_c = p.beta != 0.0f;
   auto finish = [&](int m, int c, float v) {
     const int n = col0 + c;
-    if (m < p.M && n < p.N) {
+    if (m < p.M && n >= 0 && n < p.N) {
       half* dst = p.C + static_cast<size_t>(m) * p.N + n;
       const float prev = read_c ? __half2float(*dst) : 0.0f;
       *dst = __float2half_rn(fmaf(p.alpha, v, p.beta * prev));
