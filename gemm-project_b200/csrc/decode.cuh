@@ -147,33 +147,34 @@ __global__ void __launch_bounds__(DecCfg<NM>::kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // UMMA issuer: the whole warp runs the loop, one elected lane issues.
-    // A operand = B^T (MN-major), B operand = A rows (K-major).
-    constexpr uint32_t idesc = make_idesc_f16(Cfg::BMN, NM, /*a_mn_major=*/true,
-                                              /*b_mn_major=*/false);
-    int s = 0;
-    uint32_t ph = 0;
-    for (int kb = 0; kb < num_kb; ++kb) {
-      if (!mbar_wait_warp(full_bar(s), ph, p.timeout_ns, abort_flag, p.err, kErrTimeoutMma)) break;
-      tc_fence_after();
-      const uint32_t st = sbase + s * Cfg::kStageBytes;
+    if (lane == 0) {
+      // UMMA issuer: one thread runs the loop and issues every tcgen05
+      // instruction (no per-instruction election and re-convergence).
+      // A operand = B^T (MN-major), B operand = A rows (K-major).
+      constexpr uint32_t idesc = make_idesc_f16(Cfg::BMN, NM, /*a_mn_major=*/true,
+                                                /*b_mn_major=*/false);
+      int s = 0;
+      uint32_t ph = 0;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(full_bar(s), ph, p.timeout_ns, abort_flag, p.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t st = sbase + s * Cfg::kStageBytes;
 #pragma unroll
-      for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
-        const uint64_t adesc = make_smem_desc(st + kk * 2048, Cfg::kBBoxBytes, 1024);
-        const uint64_t bdesc = make_smem_desc(st + Cfg::kBBytes + kk * 32, 16, 1024);
-        // even K steps accumulate into columns [0, NM), odd ones into [NM, 2 NM)
-        const uint32_t d = tmem_base + static_cast<uint32_t>((kk & 1) * NM);
-        if (elect_one()) umma_f16<false>(d, adesc, bdesc, idesc, (kb | (kk >> 1)) != 0 ? 1u : 0u);
-        __syncwarp();
+        for (int kk = 0; kk < Cfg::BK / 16; ++kk) {
+          const uint64_t adesc = make_smem_desc(st + kk * 2048, Cfg::kBBoxBytes, 1024);
+          const uint64_t bdesc = make_smem_desc(st + Cfg::kBBytes + kk * 32, 16, 1024);
+          // even K steps accumulate into columns [0, NM), odd ones into [NM, 2 NM)
+          const uint32_t d = tmem_base + static_cast<uint32_t>((kk & 1) * NM);
+          umma_f16<false>(d, adesc, bdesc, idesc, (kb | (kk >> 1)) != 0 ? 1u : 0u);
+        }
+        umma_commit_local<false>(empty_bar(s));
+        if (++s == Cfg::kStages) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
-      if (elect_one()) umma_commit_local<false>(empty_bar(s));
-      __syncwarp();
-      if (++s == Cfg::kStages) {
-        s = 0;
-        ph ^= 1u;
-      }
+      umma_commit_local<false>(done_bar);
     }
-    if (elect_one()) umma_commit_local<false>(done_bar);
     __syncwarp();
   }
 
