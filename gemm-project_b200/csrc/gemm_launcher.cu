@@ -72,6 +72,7 @@ struct DeviceInfo {
   int pairn_clusters = 0;         // co-resident 2-CTA clusters, 256 x 512 pair tiles
   int stream_slots = 0;           // co-resident CTAs of the TMA streaming kernels
   int dec_slots[5] = {0, 0, 0, 0, 0};  // co-resident CTAs of skinny_tc_kernel<16|32|64|128|256>
+  int split_clusters[3] = {0, 0, 0};   // co-resident (1, ks) split-K clusters, ks = 2, 4, 8
   int* err = nullptr;
   cudaMemPool_t pool = nullptr;   // repack scratch (never trimmed between calls)
   bool configured = false;
@@ -131,6 +132,29 @@ void configure_tc() {
 }
 
 // Co-resident 2-CTA clusters of a pair kernel (0 if it cannot be placed).
+// Co-resident (1, ks) clusters of the single-CTA split-K kernel (every tile
+// width takes a whole SM's shared memory, so the 128 x 128 kernel stands for all).
+int split_capacity(int sms, int ks) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(sms / ks, ks, 1);
+  cfg.blockDim = dim3(TcCfg<128, false>::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = TcCfg<128, false>::kSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = ks;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<128, false, false, 1, false>, &cfg) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  return n;
+}
+
 template <int SLABS, bool SLAB_N = false>
 int pair_capacity(int sms) {
   cudaLaunchConfig_t cfg{};
@@ -187,6 +211,7 @@ DeviceInfo& device_info() {
     configure_tc<256, true, 2>();
     configure_tc<256, true, 2, true>();
     d.pair_clusters = pair_capacity<1>(d.sms);
+    for (int i = 0; i < 3; ++i) d.split_clusters[i] = split_capacity(d.sms, 2 << i);
     d.pair2_clusters = pair_capacity<2>(d.sms);
     d.pairn_clusters = pairn_registers_ok<false>() && pairn_registers_ok<true>()
                            ? pair_capacity<2, true>(d.sms)
@@ -252,9 +277,10 @@ DeviceInfo& device_info() {
     if (env_int("GEMM_DEBUG_INFO")) {
       std::fprintf(stderr,
                    "gemm_b200 device %d: sms=%d pair_clusters=%d pair2_clusters=%d "
-                   "pairn_clusters=%d stream_slots=%d dec_slots=%d/%d/%d\n",
+                   "pairn_clusters=%d stream_slots=%d dec_slots=%d/%d/%d split_clusters=%d/%d/%d\n",
                    dev, d.sms, d.pair_clusters, d.pair2_clusters, d.pairn_clusters,
-                   d.stream_slots, d.dec_slots[0], d.dec_slots[1], d.dec_slots[2]);
+                   d.stream_slots, d.dec_slots[0], d.dec_slots[1], d.dec_slots[2],
+                   d.split_clusters[0], d.split_clusters[1], d.split_clusters[2]);
     }
     std::atomic_thread_fence(std::memory_order_release);
     d.configured = true;
@@ -326,27 +352,57 @@ constexpr int kTilePairN = 4;
 constexpr int kTileSplitK = 5;
 // A split-K CTA parks its FP32 partial (128 rows x (256 + 4) floats) in the
 // stage ring once its UMMAs are done.
-static_assert(TcCfg<256, false>::kStages * TcCfg<256, false>::kStageBytes >= 128 * 260 * 4,
+static_assert(TcCfg<256, false>::kStages * TcCfg<256, false>::kStageBytes >= 128 * 260 * 4 &&
+                  TcCfg<128, false>::kStages * TcCfg<128, false>::kStageBytes >= 128 * 132 * 4 &&
+                  TcCfg<64, false>::kStages * TcCfg<64, false>::kStageBytes >= 128 * 68 * 4,
               "split-K partial must fit the stage ring");
 
 // Split-K for small and mid-size problems: when 128 x 256 tiles are too few to
-// fill the GPU, the K range of each tile is split over a cluster (DSMEM
-// reduction). Larger tiles with split-K move far less data through L2 than many
-// small tiles: 1.4-1.7x faster for long K (e.g. 256x4096x4096: 17 instead of
-// 29 us), slower for short K, so each part keeps at least 16 K blocks.
-// Every K part holds at least one K block (num_kb > ks * (ks - 1) guarantees
-// it). GEMM_SPLITK=-1 turns it off.
-int split_k_plan(int M, int N, int K, const DeviceInfo& d) {
-  if (env_int("GEMM_SPLITK") < 0) return 1;
-  const int tiles = ceil_div(M, 128) * ceil_div(N, 256);
+// fill the GPU (at most half the SMs), the K range of each tile is split over
+// a cluster of ks CTAs whose FP32 partials are added through DSMEM. Tile width
+// and ks come from a cost model in microseconds fitted to measurements on
+// B200 (~1.85 GHz, forced plans on 15 mid-size shapes): per 64-wide K block
+// 0.24 / 0.26 / 0.36 us for the 128 x 64 / 128 x 128 / 128 x 256 tiles; the
+// reduction (partial to shared memory, two cluster barriers, the 128 x BN
+// FP32 partial across DSMEM at ~38 GB/s, C) ~3.3 us + 0.0085 us per column;
+// an unsplit tile pays its C store instead (1.5 / 2 / 2 us); 1.5 us of
+// set-up. All clusters must be co-resident (8-CTA clusters beyond the
+// capacity ran in a second wave at twice the time), and every part keeps at
+// least one K block (num_kb > ks * (ks - 1)). GEMM_SPLITK=-1 turns split-K
+// off; GEMM_SPLITK_TILE / GEMM_SPLITK_KS force a plan.
+struct SplitPlan {
+  int tile;  // 64, 128 or 256 (single-CTA tile width)
+  int ks;    // K parts per cluster; 1 = no split
+};
+
+SplitPlan split_k_plan(int M, int N, int K, const DeviceInfo& d) {
+  const SplitPlan none{256, 1};
+  if (env_int("GEMM_SPLITK") < 0) return none;
   const int num_kb = ceil_div(K, 64);
-  int ks = 1;
-  // at least 16 K blocks per part: with shorter parts the per-CTA start-up and
-  // the cluster reduction cost more than the split saves (measured at 1024^3)
-  while (ks < 8 && tiles * ks * 2 <= d.sms && num_kb >= 2 * ks * 16 &&
-         num_kb > 2 * ks * (2 * ks - 1))
-    ks *= 2;
-  return ks;
+  const int f_tile = env_int("GEMM_SPLITK_TILE"), f_ks = env_int("GEMM_SPLITK_KS");
+  if ((f_tile == 64 || f_tile == 128 || f_tile == 256) &&
+      (f_ks == 1 || f_ks == 2 || f_ks == 4 || f_ks == 8) && num_kb > f_ks * (f_ks - 1))
+    return SplitPlan{f_tile, f_ks};
+  if (ceil_div(M, 128) * ceil_div(N, 256) * 2 > d.sms) return none;  // large: the unsplit tiles
+  SplitPlan best = none;
+  float best_us = 1e30f;
+  for (const int tile : {64, 128, 256}) {
+    const int tiles = ceil_div(M, 128) * ceil_div(N, tile);
+    const float per_kb = tile == 256 ? 0.36f : (tile == 128 ? 0.26f : 0.24f);
+    const float store = tile == 64 ? 1.5f : 2.0f;
+    const float reduce = 3.3f + 0.0085f * tile;
+    for (int ks = 1; ks <= 8; ks *= 2) {
+      const int cap = ks > 1 ? d.split_clusters[ks == 2 ? 0 : (ks == 4 ? 1 : 2)] : tiles;
+      if (ks > 1 && (tiles * ks > d.sms || tiles > cap || num_kb <= ks * (ks - 1))) break;
+      const int waves = ceil_div(tiles * ks, d.sms);
+      const float us = 1.5f + waves * ceil_div(num_kb, ks) * per_kb + (ks > 1 ? reduce : store);
+      if (us < best_us) {
+        best_us = us;
+        best = SplitPlan{tile, ks};
+      }
+    }
+  }
+  return best.ks > 1 ? best : none;
 }
 
 bool tile_available(int tile, const DeviceInfo& d) {
@@ -579,13 +635,15 @@ int launch_tc(const half* A, const half* B, half* C, int M, int N, int K, float 
               cudaStream_t s, int tile, const DeviceInfo& d) {
   int ksplit = 1;
   if (tile == 0 || tile == kTileSplitK) {
-    ksplit = split_k_plan(M, N, K, d);
+    const SplitPlan plan = split_k_plan(M, N, K, d);
+    ksplit = plan.ks;
     if (tile == kTileSplitK) {
+      // a forced request: 128 x 256 tiles, split at least in two
       const int num_kb = ceil_div(K, 64);
-      if (ksplit == 1 && num_kb > 2) ksplit = 2;  // a forced request splits at least in two
+      if (plan.tile != 256 || ksplit == 1) ksplit = num_kb > 2 ? 2 : 1;
       tile = 256;
     } else if (ksplit > 1) {
-      tile = 256;
+      tile = plan.tile;
     }
   }
   if (tile != 0 && !tile_available(tile, d)) tile = 256;
@@ -845,15 +903,9 @@ int launch_col_tma(const half* A, const half* B, half* C, int M, int K, float al
 // ---------------------------------------------------------------------------
 // Small-M tensor-core path (2 <= M <= 64, TMA-addressable operands).
 // ---------------------------------------------------------------------------
-// For 64 < M <= 128 the dense path (128 x 256 tiles, split-K in a cluster when
-// the tiles are few) is faster, except when K is long against N: there the
-// small-M kernel's 128-column tiles give more CTAs (measured on B200: at
-// 96 x 4096 x 14336, 37 against 47 us; at 128 x 4096 x 4096, 23 against 16 us the
-// other way). Above M = 128 the dense path wins throughout.
-bool small_m_wins(int M, int N, int K) {
-  return M <= 128 && static_cast<long long>(K) >= 3ll * N;
-}
-
+// For M > 64 the dense path (with split-K over narrower tiles when the tiles
+// are few) is faster: measured on B200, 128 x 1024 x 8192 10.1 against 16.8 us,
+// 128 x 4096 x 4096 10.5 against 22.3 us.
 bool dec_ok(const half* A, const half* B, int M, int N, int K, const DeviceInfo& d) {
   return d.dec_slots[0] > 0 && M >= 1 && M <= 256 && aligned16(A) && aligned16(B) && K % 8 == 0 &&
          N % 8 == 0;
@@ -935,7 +987,7 @@ int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float a
   if (path == 0) {
     if (M == 1 || (M == 2 && rows_tma_ok(A, B, M, N, K, d)))
       path = 2;                       // streaming GEMV (M = 2: faster than the tensor-core kernel)
-    else if (N > 1 && dec_ok(A, B, M, N, K, d) && (M <= 64 || small_m_wins(M, N, K)))
+    else if (N > 1 && M <= 64 && dec_ok(A, B, M, N, K, d))
       path = 6;                       // small-M tensor-core kernel
     else if (M <= 8)
       path = 2;                       // misaligned small M: per-thread loads

@@ -124,8 +124,8 @@ struct TcCfg {
   // shares must fit in what the block is launched with (kThreads x the
   // kernel's register count); the launcher checks this before using the tile.
   // Split-K (the K range of a tile over a cluster, FP32 partials added through
-  // DSMEM) exists for the single-CTA 128 x 256 tile.
-  static constexpr bool kSplitK = BN_ == 256 && !PAIR_ && SLABS_ == 1 && !SLAB_N_;
+  // DSMEM) exists for the single-CTA tiles (128 x 64, 128 x 128, 128 x 256).
+  static constexpr bool kSplitK = !PAIR_ && SLABS_ == 1 && !SLAB_N_;
   static constexpr int kRegsCtl = 48;
   static constexpr int kRegsEpi = 224;
   static constexpr int kRegSplitTotal = 128 * kRegsCtl + 32 * kEpiWarps * kRegsEpi;

@@ -73,6 +73,20 @@ def test_split_k_cluster(lib, cuda, shape, beta):
     _go(lib, cuda, m, n, k, 0.75, beta, dist="normal", path=PATH_TC, tile_n=5, seed=m + 7 * k)
 
 
+# Split-K on every single-CTA tile width, plans forced through the planner's
+# override: ragged M, N and K, beta != 0, a misaligned C (scalar stores).
+@pytest.mark.parametrize("tile,ks", [(64, 2), (64, 4), (128, 2), (128, 4), (128, 8), (256, 8)],
+                         ids=str)
+@pytest.mark.parametrize("shape,c_off", [((300, 1000, 4104), 0), ((256, 1024, 4096), 0),
+                                         ((700, 900, 3000), 1), ((96, 4096, 1000), 0)], ids=str)
+def test_split_k_tile_widths(lib, cuda, monkeypatch, tile, ks, shape, c_off):
+    monkeypatch.setenv("GEMM_SPLITK_TILE", str(tile))
+    monkeypatch.setenv("GEMM_SPLITK_KS", str(ks))
+    m, n, k = shape
+    _go(lib, cuda, m, n, k, 0.75, -0.5, dist="normal", path=PATH_TC, offsets=(0, 0, c_off),
+        seed=tile + ks + m)
+
+
 def test_split_k_misaligned_c(lib, cuda):
     _go(lib, cuda, 700, 900, 3000, 0.75, 0.25, path=PATH_TC, tile_n=5, offsets=(0, 0, 1), seed=3)
 
@@ -236,11 +250,11 @@ def test_dispatch_choices(lib, cuda):
     assert names[(3, 5000, 4097)].startswith("rows_tma_kernel<4,a-direct>")
     run(lib, cuda, 8, 6144, 4096, fn="launcher")
     assert gemm_b200.last_kernel().startswith("skinny_tc_kernel<16>")
-    # 64 < M <= 128 with K >= 3N: the small-M kernel; otherwise the dense path, whose
-    # 128 x 256 tiles split K over a cluster when they are too few to fill the GPU
+    # M > 64: the dense path, whose single-CTA tiles split K over a cluster when
+    # they are too few to fill the GPU (128 x 128 tiles, 4 parts, here)
     run(lib, cuda, 96, 4096, 14336, fn="launcher")
-    assert gemm_b200.last_kernel().startswith("skinny_tc_kernel<128>")
+    assert gemm_b200.last_kernel().startswith("tc_gemm_kernel")
     run(lib, cuda, 128, 4096, 4096, fn="launcher")
-    assert gemm_b200.last_kernel().startswith("tc_gemm_kernel<128x256>")
+    assert gemm_b200.last_kernel().startswith("tc_gemm_kernel<128x128>")
     run(lib, cuda, 200, 4096, 8192, fn="launcher")
     assert gemm_b200.last_kernel().startswith("tc_gemm_kernel")
