@@ -151,6 +151,81 @@ def gemm_sub(a, b, c, alpha: float = 1.0, beta: float = 0.0, stream=None, max_sm
                         f"(pitches {a.stride(0)}, {b.stride(0)}, {c.stride(0)})")
 
 
+_host_streams: dict = {}
+
+
+def gemm_host(a, b, c, alpha: float = 1.0, beta: float = 0.0, out=None, slabs: int = 8,
+              stream=None):
+    """C = half(alpha * A@B + beta * C) for operands in HOST memory, computed on
+    the current CUDA device; the result goes to `out` (a host tensor, default c).
+
+    The transfers are pipelined over row slabs on three streams: B crosses to
+    the device first, then each slab's rows of A (and of C when beta != 0);
+    each slab's GEMM starts as soon as its rows have landed, and its rows of C
+    go back while later slabs still travel. PCIe carries both directions at
+    once, so a call costs about its host-to-device bytes / PCIe bandwidth
+    instead of the sum of all transfers and the GEMM. Pinned host tensors are
+    needed for the copies to overlap (pageable ones work, synchronously).
+    Asynchronous like the device entry points: `stream` (a torch.cuda.Stream;
+    default: the current stream) is ordered after the last copy back;
+    synchronize it before reading `out`.
+    """
+    import torch
+    for name, t in (("A", a), ("B", b), ("C", c)) + ((("out", out),) if out is not None else ()):
+        if t.dtype != torch.float16 or t.is_cuda or t.dim() != 2 or not t.is_contiguous():
+            raise GemmError(f"{name} must be a contiguous 2-D float16 host tensor")
+    m, k = a.shape
+    k2, n = b.shape
+    if k2 != k or tuple(c.shape) != (m, n) or (out is not None and tuple(out.shape) != (m, n)):
+        raise GemmError(f"shape mismatch A{tuple(a.shape)} B{tuple(b.shape)} C{tuple(c.shape)}")
+    if out is None:
+        out = c
+    if m == 0 or n == 0:
+        return out
+    dev = torch.device("cuda", torch.cuda.current_device())
+    caller = torch.cuda.current_stream(dev) if stream is None else stream
+    if dev.index not in _host_streams:
+        _host_streams[dev.index] = tuple(torch.cuda.Stream(dev) for _ in range(3))
+    h2d, comp, d2h = _host_streams[dev.index]
+    read_c = beta != 0.0
+    # slabs of whole 128-row tiles (one slab for small M)
+    if m < 256 or slabs <= 1:
+        rows = m
+    else:
+        rows = max(128, (-(-m // slabs)) // 128 * 128)
+    bounds = [(r, min(m, r + rows)) for r in range(0, m, rows)]
+    a_d = torch.empty((m, k), dtype=torch.float16, device=dev)
+    b_d = torch.empty((k, n), dtype=torch.float16, device=dev)
+    c_d = torch.empty((m, n), dtype=torch.float16, device=dev)
+    for t in (a_d, b_d, c_d):  # used on the side streams: keep them alive until those finish
+        for s in (h2d, comp, d2h):
+            t.record_stream(s)
+    h2d.wait_stream(caller)
+    b_done = torch.cuda.Event()
+    with torch.cuda.stream(h2d):
+        b_d.copy_(b, non_blocking=True)
+        b_done.record(h2d)
+    done = None
+    for r0, r1 in bounds:
+        landed, computed = torch.cuda.Event(), torch.cuda.Event()
+        with torch.cuda.stream(h2d):
+            a_d[r0:r1].copy_(a[r0:r1], non_blocking=True)
+            if read_c:
+                c_d[r0:r1].copy_(c[r0:r1], non_blocking=True)
+            landed.record(h2d)
+        comp.wait_event(b_done)
+        comp.wait_event(landed)
+        gemm(a_d[r0:r1], b_d, c_d[r0:r1], alpha, beta, stream=comp)
+        computed.record(comp)
+        d2h.wait_event(computed)
+        with torch.cuda.stream(d2h):
+            out[r0:r1].copy_(c_d[r0:r1], non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(d2h)
+    caller.wait_event(done)
+    return out
+
+
 def gemm_tn(a, bt, c, alpha: float = 1.0, beta: float = 0.0, stream=None, tile_n: int = 0) -> None:
     """C = half(alpha * A @ Bt.T + beta * C) with Bt[N,K] (a linear layer's weight layout)."""
     lib = load()
