@@ -8,8 +8,8 @@
 // kernels:
 //   K <= 0                      -> scale_c_kernel (C = beta*C)
 //   M == 1 (and M == 2)         -> rows_tma_kernel<MR>   (TMA-fed HBM streaming, cluster split-K)
-//   2 <= M <= 64, TMA-friendly  -> skinny_tc_kernel<NM>  (tcgen05, C^T = B^T A^T, cluster split-K)
-//   64 < M <= 128, K >= 3N, TMA-friendly            -> skinny_tc_kernel<128>
+//   2 <= M <= 32, TMA-friendly  -> skinny_tc_kernel<NM>  (tcgen05, C^T = B^T A^T, cluster split-K)
+//   32 < M <= 64, TMA-friendly, many output tiles   -> skinny_tc_kernel<64>
 //   M <= 8 otherwise, N % 8 == 0 -> rows_tma_kernel<MR>  (B from its 16-byte line with a
 //                                   column phase; A direct when not TMA-addressable, M <= 4)
 //   M <= 8 otherwise            -> rows_gemv_kernel<MR>  (per-thread loads, any alignment)
@@ -217,13 +217,16 @@ DeviceInfo& device_info() {
                            ? pair_capacity<2, true>(d.sms)
                            : 0;
     {
-      cudaFuncSetAttribute(rows_tma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
-      cudaFuncSetAttribute(rows_tma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
-      cudaFuncSetAttribute(rows_tma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
-      cudaFuncSetAttribute(rows_tma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
-      cudaFuncSetAttribute(rows_tma_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
-      cudaFuncSetAttribute(rows_tma_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
-      cudaFuncSetAttribute(rows_tma_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
+      const auto rows_smem = [](auto kernel) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemBytes);
+      };
+      rows_smem(rows_tma_kernel<1>);
+      rows_smem(rows_tma_kernel<2>);
+      rows_smem(rows_tma_kernel<4>);
+      rows_smem(rows_tma_kernel<8>);
+      rows_smem(rows_tma_kernel<1, false>);
+      rows_smem(rows_tma_kernel<2, false>);
+      rows_smem(rows_tma_kernel<4, false>);
       cudaFuncSetAttribute(col_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kColSmemBytes);
       // Co-resident CTAs of both streaming kernels (the smaller of the two).
       int per_sm = 0, per_sm_col = 0;
@@ -370,6 +373,11 @@ static_assert(TcCfg<256, false>::kStages * TcCfg<256, false>::kStageBytes >= 128
 // capacity ran in a second wave at twice the time), and every part keeps at
 // least one K block (num_kb > ks * (ks - 1)). GEMM_SPLITK=-1 turns split-K
 // off; GEMM_SPLITK_TILE / GEMM_SPLITK_KS force a plan.
+// Few enough 128 x 256 tiles (at most half the SMs) for split-K to pay.
+bool few_dense_tiles(int M, int N, const DeviceInfo& d) {
+  return static_cast<long long>(ceil_div(M, 128)) * ceil_div(N, 256) * 2 <= d.sms;
+}
+
 struct SplitPlan {
   int tile;  // 64, 128 or 256 (single-CTA tile width)
   int ks;    // K parts per cluster; 1 = no split
@@ -383,7 +391,7 @@ SplitPlan split_k_plan(int M, int N, int K, const DeviceInfo& d) {
   if ((f_tile == 64 || f_tile == 128 || f_tile == 256) &&
       (f_ks == 1 || f_ks == 2 || f_ks == 4 || f_ks == 8) && num_kb > f_ks * (f_ks - 1))
     return SplitPlan{f_tile, f_ks};
-  if (ceil_div(M, 128) * ceil_div(N, 256) * 2 > d.sms) return none;  // large: the unsplit tiles
+  if (!few_dense_tiles(M, N, d)) return none;  // large: the unsplit tiles
   SplitPlan best = none;
   float best_us = 1e30f;
   for (const int tile : {64, 128, 256}) {
@@ -905,7 +913,11 @@ int launch_col_tma(const half* A, const half* B, half* C, int M, int K, float al
 // ---------------------------------------------------------------------------
 // For M > 64 the dense path (with split-K over narrower tiles when the tiles
 // are few) is faster: measured on B200, 128 x 1024 x 8192 10.1 against 16.8 us,
-// 128 x 4096 x 4096 10.5 against 22.3 us.
+// 128 x 4096 x 4096 10.5 against 22.3 us. For 32 < M <= 64 it is faster when
+// split-K applies (64 x 4096 x 4096 10.5 against 12.9 us, 64 x 14336 x 4096
+// 25.4 against 30.9 us) and slower on large HBM-bound shapes (64 x 28672 x
+// 8192 83.8 against 74.0 us); up to M = 32 the small-M kernel is as fast or
+// faster (16 x 4096 x 4096 8.8 against 10.2 us).
 bool dec_ok(const half* A, const half* B, int M, int N, int K, const DeviceInfo& d) {
   return d.dec_slots[0] > 0 && M >= 1 && M <= 256 && aligned16(A) && aligned16(B) && K % 8 == 0 &&
          N % 8 == 0;
@@ -987,7 +999,8 @@ int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float a
   if (path == 0) {
     if (M == 1 || (M == 2 && rows_tma_ok(A, B, M, N, K, d)))
       path = 2;                       // streaming GEMV (M = 2: faster than the tensor-core kernel)
-    else if (N > 1 && M <= 64 && dec_ok(A, B, M, N, K, d))
+    else if (N > 1 && M <= 64 && dec_ok(A, B, M, N, K, d) &&
+             (M <= 32 || !few_dense_tiles(M, N, d)))
       path = 6;                       // small-M tensor-core kernel
     else if (M <= 8)
       path = 2;                       // misaligned small M: per-thread loads

@@ -250,6 +250,11 @@ def test_dispatch_choices(lib, cuda):
     assert names[(3, 5000, 4097)].startswith("rows_tma_kernel<4,a-direct>")
     run(lib, cuda, 8, 6144, 4096, fn="launcher")
     assert gemm_b200.last_kernel().startswith("skinny_tc_kernel<16>")
+    # 32 < M <= 64: split-K dense tiles when the output tiles are few, else small-M
+    run(lib, cuda, 48, 4096, 4096, fn="launcher")
+    assert gemm_b200.last_kernel().startswith("tc_gemm_kernel<128x128>")
+    run(lib, cuda, 48, 28672, 1024, fn="launcher")
+    assert gemm_b200.last_kernel().startswith("skinny_tc_kernel<64>")
     # M > 64: the dense path, whose single-CTA tiles split K over a cluster when
     # they are too few to fill the GPU (128 x 128 tiles, 4 parts, here)
     run(lib, cuda, 96, 4096, 14336, fn="launcher")
