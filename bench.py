@@ -5,11 +5,19 @@ Workloads:
             (the config the headline TFLOP/s metric is quoted on). The same line
             carries the other single-GPU configs under "configs": the M=1 and N=1
             GEMVs (GB/s), 4096^3, 1024^3 and the odd/misaligned shapes, each next to
-            cuBLAS on the same inputs.
+            cuBLAS on the same inputs, three ways: per call (ctypes launches back to
+            back), device time (the calls replayed from a CUDA graph, so no host
+            launch gap counts) and cold (L2 evicted by a 512 MiB write before
+            every call, the reference's square_benchmark.cu:134-152 method).
   N > 1   : the sharded 32768 x 32768 x 16384 GEMM, weak-scaled: every rank owns a
             4096-row C slab (4096 x 32768 x 16384 per rank, the 8-GPU partition of
             the config); B is generated on rank 0 and broadcast once over NCCL
             (timed separately, outside the steps); no collective inside a step.
+            The line also carries: every rank's results checked against the CPU
+            oracle (256 sampled rows and 64 FP64 spots per rank), the per-GPU
+            efficiency against the same slab timed on one GPU alone in the same
+            run, and the strong-scaling time of the fixed 32768-row problem with
+            the broadcast of B overlapped with the GEMM.
 A step is one gemm_launcher call over the workload. Inputs are larger than the
 126 MB L2 (no flush needed). Times are CUDA events on the launching stream,
 max over ranks.
@@ -17,7 +25,8 @@ max over ranks.
 `--impl reference` times the reference's CPU path for the same config on the host
 cores: its tests' check formula alpha*(A.float()@B.float()) + beta*C.float()
 (tests/test_gemm.py:91,130,156) in torch FP32 on the CPU, each step a bounded
-sample of rows of the same GEMM.
+sample of rows of the same GEMM. The CPU baseline in this arm's own line is
+measured with the same function, rows and warm-up.
 """
 from __future__ import annotations
 
@@ -26,7 +35,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -40,6 +48,8 @@ sys.path.insert(0, str(PKG))
 os.environ.setdefault("GEMM_LAUNCH_LOG", "0")
 
 L2_BYTES = 126 * 1024 * 1024
+FLUSH_BYTES = 512 << 20          # >= 4x the L2: the cold-L2 eviction write
+CPU_SAMPLE_ROWS = 1024           # rows of the CPU baseline sample (both arms)
 METRIC = "FP16 GEMM TFLOP/s (% dense peak) at 8192³; M=1 GEMV GB/s vs HBM peak"
 
 
@@ -52,14 +62,32 @@ def peaks():
     return {"hbm_gbs": 6650.0, "tflops": 1590.0, "tflops_sustained": 1400.0, "source": "fallback"}
 
 
+def workload_config(world: int, cfgs) -> dict:
+    """The `config` of both arms (identical keys and values, so that the two
+    lines describe the same workload)."""
+    if world > 1:
+        cfg = cfgs["sharded32768"]
+        return {"workload": "sharded FP16 GEMM, 4096-row C slab per rank of the "
+                            "32768x32768x16384 config (BASELINE configs[4]); M = 4096 x n_gpus",
+                "M": 4096 * world, "N": cfg["n"], "K": cfg["k"], "alpha": cfg["alpha"],
+                "beta": cfg["beta"], "parallelism": f"C row slabs x{world}, B broadcast once",
+                "l2": "inputs larger than the 126 MB L2; no flush"}
+    cfg = cfgs["square8192"]
+    return {"workload": "square FP16 GEMM M=N=K=8192, alpha=1, beta=0.5 (BASELINE configs[1])",
+            "M": cfg["m"], "N": cfg["n"], "K": cfg["k"], "alpha": cfg["alpha"],
+            "beta": cfg["beta"], "parallelism": "none (one device)",
+            "l2": "inputs (384 MiB) larger than the 126 MB L2; no flush"}
+
+
 # ---------------------------------------------------------------------------
-# clocks sampler (NVML, every few ms, during the timed region)
+# clocks sampler (NVML, every few ms, during the timed region only)
 # ---------------------------------------------------------------------------
 class ClockSampler:
     """SM clock, power and clock-event (throttle) reasons of one GPU, polled
     through NVML (the data nvidia-smi's clocks line reads) every `period_s`
-    from a thread while the timed region runs: timed regions of tens of
-    milliseconds still get samples. Reading only; no GPU setting is touched."""
+    from a thread. The `with` block is the timed region itself: sampling
+    starts at its entry and stops at its exit, so every sample falls inside
+    it. Reading only; no GPU setting is touched."""
 
     REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
                ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
@@ -67,7 +95,7 @@ class ClockSampler:
                ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"),
                ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, device, period_s: float = 0.005):
+    def __init__(self, device, period_s: float = 0.002):
         self.device = device
         self.period = period_s
         self.sm: list[float] = []
@@ -75,7 +103,9 @@ class ClockSampler:
         self.reasons: set[str] = set()
         self.max_mhz = None
         self._stop = threading.Event()
+        self._started = threading.Event()
         self._handle = None
+        self.t_start = self.t_end = None
 
     def _open(self):
         import pynvml
@@ -97,10 +127,13 @@ class ClockSampler:
             return self
         self.thread = threading.Thread(target=self._run, daemon=True)
         self.thread.start()
+        self._started.wait(1.0)
+        self.t_start = time.perf_counter()
         return self
 
     def _run(self):
         nv, h = self.nvml, self._handle
+        self._started.set()
         while not self._stop.is_set():
             try:
                 self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
@@ -114,16 +147,19 @@ class ClockSampler:
             self._stop.wait(self.period)
 
     def __exit__(self, *exc):
+        self.t_end = time.perf_counter()
         self._stop.set()
         if self._handle is not None:
             self.thread.join(timeout=2)
 
     def summary(self):
+        window = (self.t_end - self.t_start) if self.t_start and self.t_end else None
         return {"sm_mhz": statistics.median(self.sm) if self.sm else None,
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
                 "samples": len(self.sm),
                 "power_w": round(statistics.median(self.power), 1) if self.power else None,
-                "source": "NVML, sampled every 5 ms during the timed region"}
+                "window_s": round(window, 4) if window else None,
+                "source": "NVML every 2 ms, only inside the timed region"}
 
 
 # ---------------------------------------------------------------------------
@@ -175,20 +211,20 @@ def warm_up(fn, calls, seconds):
     return n
 
 
-def time_block(fn, steps, stream):
-    """ms per call over `steps` back-to-back calls, CUDA events on `stream`."""
+def time_block(fn, steps):
+    """ms per call over `steps` back-to-back calls, CUDA events on the current stream."""
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    start.record(stream)
+    start.record()
     for _ in range(steps):
         fn()
-    end.record(stream)
+    end.record()
     torch.cuda.synchronize()
     return start.elapsed_time(end) / steps
 
 
-def paired_ms(fn_ours, fn_ref, steps, warmup, stream, rounds=5, warm_s=0.5):
+def paired_ms(fn_ours, fn_ref, steps, warmup, rounds=5, warm_s=0.5):
     """Median ms per call of two implementations timed in alternating blocks
     (ours, ref, ours, ref, ...) after both are warm, so that both see the same
     power-capped clock (on a 1 kW B200 it drifts with temperature)."""
@@ -196,23 +232,83 @@ def paired_ms(fn_ours, fn_ref, steps, warmup, stream, rounds=5, warm_s=0.5):
     warm_up(fn_ref, warmup, warm_s / 4)
     t_ours, t_ref = [], []
     for _ in range(rounds):
-        t_ours.append(time_block(fn_ours, steps, stream))
-        t_ref.append(time_block(fn_ref, steps, stream))
+        t_ours.append(time_block(fn_ours, steps))
+        t_ref.append(time_block(fn_ref, steps))
     return statistics.median(t_ours), statistics.median(t_ref)
 
 
-def time_calls(fn, steps, warmup, stream, warm_s=0.5):
-    """Average ms per call over `steps` back-to-back calls (CUDA events on
-    `stream`), after warm_up(fn, warmup, warm_s)."""
-    warm_up(fn, warmup, warm_s)
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(steps):
-        fn()
-    end.record(stream)
+def capture_graph(fn, reps):
+    """A CUDA graph of `reps` back-to-back calls of fn (which launches on the
+    current stream)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            fn()
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
+        for _ in range(reps):
+            fn()
     torch.cuda.synchronize()
-    return start.elapsed_time(end) / steps
+    return g
+
+
+def paired_device_ms(fn_ours, fn_ref, reps, rounds=5):
+    """Device ms per call of two implementations: each one's calls captured in
+    a CUDA graph and replayed in alternating blocks (no host launch gaps, same
+    clock for both). Returns (ours, ref); None for one that cannot be captured."""
+    graphs = []
+    for fn in (fn_ours, fn_ref):
+        try:
+            graphs.append(capture_graph(fn, reps))
+        except Exception:
+            torch.cuda.synchronize()
+            graphs.append(None)
+    times = [[], []]
+    for g in graphs:
+        if g is not None:
+            g.replay()
+    torch.cuda.synchronize()
+    for _ in range(rounds):
+        for i, g in enumerate(graphs):
+            if g is None:
+                continue
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            times[i].append(e0.elapsed_time(e1) / reps)
+    return tuple(statistics.median(t) if t else None for t in times)
+
+
+class L2Flush:
+    """Cold-L2 timing: a 512 MiB write (>= 4x the 126 MB L2) before every timed
+    call evicts the operands, as the reference's square benchmark does with its
+    eviction sweep (benchmarks/square_benchmark.cu:134-152, around every
+    profiled trial at :164-172). The write takes ~0.1 ms on the device, longer
+    than the host needs to enqueue the timed call, so the call's start event
+    follows the flush without a host gap."""
+
+    def __init__(self, device):
+        self.buf = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=device)
+
+    def paired_cold_ms(self, fn_ours, fn_ref, trials=15):
+        """Median ms of single calls, L2 evicted before each; ours and ref interleaved."""
+        fn_ours()
+        fn_ref()
+        evs = [[], []]
+        for i in range(trials):
+            for j, fn in enumerate((fn_ours, fn_ref)):
+                self.buf.fill_(i)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                evs[j].append((e0, e1))
+        torch.cuda.synchronize()
+        return tuple(statistics.median(e0.elapsed_time(e1) for e0, e1 in ev) for ev in evs)
 
 
 def traffic_from_profile(name: str):
@@ -230,45 +326,50 @@ def traffic_from_profile(name: str):
     return None
 
 
-def cpu_reference_rate(m, n, k, dist, alpha, beta, budget_s=8.0, threads=None):
-    """Time the reference's CPU check formula on a bounded row sample of the
-    same GEMM; returns (TFLOP/s, rows, seconds, threads)."""
+def cpu_formula_rate(m, n, k, dist, alpha, beta, rows, steps, warmup, threads):
+    """The reference's CPU check formula alpha*(A.float()@B.float()) + beta*C.float()
+    (tests/test_gemm.py:91,130,156) timed on `threads` host threads over a
+    sample of `rows` rows of the same GEMM (seed 0): `warmup` untimed calls,
+    then `steps` timed calls. Both arms of this benchmark use this function
+    with the same rows and warm-up. Returns (TFLOP/s, ms per call, rows)."""
     sys.path.insert(0, str(REPO))
     from oracle import oracle
-    threads = threads or oracle.cpu_threads()
     torch.set_num_threads(threads)
-    rows = min(m, 256)
+    rows = min(m, rows)
     a, b, c = oracle.make_inputs(rows, n, k, dist, seed=0)
-    oracle.reference_fp32(a, b, c, alpha, beta)  # warm up BLAS
-    t0 = time.perf_counter()
-    oracle.reference_fp32(a, b, c, alpha, beta)
-    dt = time.perf_counter() - t0
-    # grow the sample to about budget_s of CPU work
-    target_rows = int(min(m, max(rows, rows * budget_s / max(dt, 1e-6) / 2)))
-    if target_rows > rows:
-        a, b, c = oracle.make_inputs(target_rows, n, k, dist, seed=0)
-        rows = target_rows
-    reps, total = 0, 0.0
-    while total < budget_s / 2 or reps < 1:
-        t0 = time.perf_counter()
+    for _ in range(max(warmup, 1)):
         oracle.reference_fp32(a, b, c, alpha, beta)
-        total += time.perf_counter() - t0
-        reps += 1
-    tflops = 2.0 * rows * n * k * reps / total / 1e12
-    return tflops, rows, total, threads
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        oracle.reference_fp32(a, b, c, alpha, beta)
+    ms = (time.perf_counter() - t0) / steps * 1e3
+    return 2.0 * rows * n * k / (ms * 1e-3) / 1e12, ms, rows
+
+
+def cpu_threads():
+    sys.path.insert(0, str(REPO))
+    from oracle import oracle
+    return oracle.cpu_threads()
+
+
+def r3(x):
+    return None if x is None else round(float(x), 3)
 
 
 # ---------------------------------------------------------------------------
 # single-GPU workloads
 # ---------------------------------------------------------------------------
-def measure_config(gb, name, cfg, stream, steps, warmup, device, tn=False):
+def measure_config(gb, name, cfg, steps, warmup, device, flush=None, tn=False):
+    """One config next to cuBLAS on the same inputs: per call (back-to-back
+    ctypes calls), device time (CUDA graph replay), and cold-L2 single calls."""
     m, n, k = cfg["m"], cfg["n"], cfg["k"]
     a, b, c = dev_inputs(m, n, k, cfg["dist"], cfg.get("c_dist", "uniform"), 0, device)
     if tn:  # the same product with B given as Bt[N,K] (gemm_launcher_tn)
         bt = b.t().contiguous()
         c_t = c.clone()
-        ms_t = time_calls(lambda: gb.gemm_tn(a, bt, c_t, cfg["alpha"], cfg["beta"], stream), steps,
-                          warmup, stream)
+        fn = lambda: gb.gemm_tn(a, bt, c_t, cfg["alpha"], cfg["beta"])  # noqa: E731
+        warm_up(fn, warmup, 0.5)
+        ms_t = time_block(fn, steps)
         return {"M": m, "N": n, "K": k, "kernel": gb.last_kernel(), "us": ms_t * 1e3,
                 "tflops": 2.0 * m * n * k / ms_t / 1e9}
     off = cfg.get("offset", 0)
@@ -276,38 +377,58 @@ def measure_config(gb, name, cfg, stream, steps, warmup, device, tn=False):
     alpha, beta = cfg["alpha"], cfg["beta"]
     c_ours = c.clone() if off == 0 else offset_copy(c, off)
     c_cub = c.clone()
-    ms, ms_cub = paired_ms(lambda: gb.gemm(a, b, c_ours, alpha, beta, stream),
-                           lambda: gb.cublas(a, b, c_cub, alpha, beta, stream), steps, warmup, stream)
-    gb.gemm(a, b, c_ours, alpha, beta, stream)
+    ours = lambda: gb.gemm(a, b, c_ours, alpha, beta)  # noqa: E731
+    cub = lambda: gb.cublas(a, b, c_cub, alpha, beta)  # noqa: E731
+    ms, ms_cub = paired_ms(ours, cub, steps, warmup)
+    ours()
     kernel = gb.last_kernel()
+    st = gb.status()
+    if st != 0:
+        raise RuntimeError(f"library status {st} in config {name}")
+    dev_ms, dev_cub = paired_device_ms(ours, cub, reps=max(3, min(steps, 20)))
+    if gb.status() != 0:
+        # a call refused inside the graph capture (its error is in the status):
+        # the graph does not hold the work, so it yields no device time
+        dev_ms = None
+    cold = flush.paired_cold_ms(ours, cub) if flush is not None else (None, None)
+    st = gb.status()
+    if st != 0:
+        raise RuntimeError(f"library status {st} in config {name}")
     flops = 2.0 * m * n * k
     bytes_ = 2.0 * (m * k + k * n + m * n) + (2.0 * m * n if beta != 0 else 0.0)
-    return {"M": m, "N": n, "K": k, "kernel": kernel, "us": ms * 1e3, "cublas_us": ms_cub * 1e3,
-            "tflops": flops / ms / 1e9, "gbs": bytes_ / ms / 1e6,
-            "cublas_tflops": flops / ms_cub / 1e9, "cublas_gbs": bytes_ / ms_cub / 1e6,
-            "vs_cublas": ms_cub / ms}
+    best = dev_ms or ms
+    out = {"M": m, "N": n, "K": k, "kernel": kernel,
+           "us": r3(ms * 1e3), "device_us": r3(dev_ms and dev_ms * 1e3),
+           "cold_us": r3(cold[0] and cold[0] * 1e3),
+           "cublas_us": r3(ms_cub * 1e3), "cublas_device_us": r3(dev_cub and dev_cub * 1e3),
+           "cublas_cold_us": r3(cold[1] and cold[1] * 1e3),
+           "tflops": r3(flops / best / 1e9), "gbs": r3(bytes_ / best / 1e6),
+           "vs_cublas_call": r3(ms_cub / ms),
+           "vs_cublas_device": r3(dev_cub / dev_ms) if dev_ms and dev_cub else None,
+           "vs_cublas_cold": r3(cold[1] / cold[0]) if cold[0] and cold[1] else None}
+    return out
 
 
-def run_single(args, gb, oracle_cfgs, device, pk):
+def run_single(args, gb, cfgs, device, pk):
     stream = torch.cuda.current_stream()
-    cfg = oracle_cfgs["square8192"]
+    cfg = cfgs["square8192"]
     m, n, k, alpha, beta = cfg["m"], cfg["n"], cfg["k"], cfg["alpha"], cfg["beta"]
     a, b, c = dev_inputs(m, n, k, "normal", "uniform", 0, device)
     flops = 2.0 * m * n * k
     steps, warmup = args.steps, max(args.warmup, 3)
+    step = lambda: gb.gemm(a, b, c, alpha, beta)  # noqa: E731
     # warm-up (untimed): at least `warmup` steps and one second, to steady clocks
-    warm_run = warm_up(lambda: gb.gemm(a, b, c, alpha, beta, stream), warmup, 1.0)
+    warm_run = warm_up(step, warmup, 1.0)
     kernel = gb.last_kernel()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
     with ClockSampler(device) as clk:
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
         start.record(stream)
         for _ in range(steps):
-            gb.gemm(a, b, c, alpha, beta, stream)
+            step()
         end.record(stream)
         torch.cuda.synchronize()
-        time.sleep(0.25)
     ms = start.elapsed_time(end) / steps
     st = gb.status()
     if st != 0:
@@ -326,78 +447,138 @@ def run_single(args, gb, oracle_cfgs, device, pk):
         gb.gemm_host(a_h, b_h, c_h, alpha, beta, out=c_out, stream=stream)
 
     e2e_steps = max(3, min(steps, 10))
-    e2e_ms = time_calls(e2e_step, e2e_steps, 2, stream)
+    warm_up(e2e_step, 2, 0.0)
+    e2e_ms = time_block(e2e_step, e2e_steps)
     h2d = (a.numel() + b.numel() + c.numel()) * 2
     d2h = c.numel() * 2
 
     # cuBLAS on the same inputs, in blocks alternating with ours (the ratio's basis)
-    ms_pair, ms_cub = paired_ms(lambda: gb.gemm(a, b, c, alpha, beta, stream),
-                                lambda: gb.cublas(a, b, c, alpha, beta, stream), steps, warmup,
-                                stream)
+    ms_pair, ms_cub = paired_ms(step, lambda: gb.cublas(a, b, c, alpha, beta), steps, warmup)
 
     # other single-GPU configs (each next to cuBLAS on the same inputs)
     configs = {}
     if not args.quick:
+        flush = L2Flush(device)
         for name in ["square4096", "square1024", "gemv_m1", "gemv_n1", "odd_1023", "odd_3"]:
             reps = 20 if name != "square4096" else 10
-            configs[name] = measure_config(gb, name, oracle_cfgs[name], stream, reps, 5, device)
+            cold = flush if name in ("square4096", "square1024", "odd_1023", "odd_3") else None
+            configs[name] = measure_config(gb, name, cfgs[name], reps, 5, device, flush=cold)
+        del flush
         # the per-rank slab of the sharded config on one GPU, for the scaling comparison
-        sl = dict(oracle_cfgs["sharded32768"], m=4096)
-        configs["slab4096x32768x16384"] = measure_config(gb, "slab", sl, stream, 3, 2, device)
+        sl = dict(cfgs["sharded32768"], m=4096)
+        configs["slab4096x32768x16384"] = measure_config(gb, "slab", sl, 3, 2, device)
         for key, prof in (("gemv_m1", "rows_tma_gemv_m1"), ("gemv_n1", "col_tma_gemv_n1")):
-            configs[key]["hbm_frac"] = configs[key]["gbs"] / pk["hbm_gbs"]
-            configs[key]["hbm_frac_unit"] = f"of {pk['source']} {pk['hbm_gbs']} GB/s copy"
+            configs[key]["hbm_frac"] = r3(configs[key]["gbs"] / pk["hbm_gbs"])
             configs[key]["traffic"] = traffic_from_profile(prof)
 
     traffic = traffic_from_profile("tc_gemm_8192")
     tflop_peak = pk["tflops"]
-    roof = {"bound": "tensor", "achieved": value, "peak": tflop_peak, "unit": "TFLOP/s",
-            "frac": value / tflop_peak, "traffic": traffic,
+    roof = {"bound": "tensor", "achieved": round(value, 2), "peak": tflop_peak, "unit": "TFLOP/s",
+            "frac": round(value / tflop_peak, 4), "traffic": traffic,
             "kernel": kernel, "peak_source": f"{pk['source']} cuBLAS bf16 burst",
             "algorithmic_flop_per_launch": flops,
-            "frac_of_nominal_2250": value / 2250.0}
-    tflops_cpu, rows, secs, threads = cpu_reference_rate(m, n, k, "normal", alpha, beta,
-                                                          budget_s=args.cpu_budget)
+            "frac_of_sustained": (round(value / pk["tflops_sustained"], 4)
+                                  if pk.get("tflops_sustained") else None),
+            "frac_of_nominal_2250": round(value / 2250.0, 4)}
+    threads = cpu_threads()
+    cpu_steps = 3
+    tf_all, ms_all, rows = cpu_formula_rate(m, n, k, "normal", alpha, beta, CPU_SAMPLE_ROWS,
+                                            cpu_steps, 2, threads)
+    tf_4, ms_4, _ = cpu_formula_rate(m, n, k, "normal", alpha, beta, CPU_SAMPLE_ROWS, 1, 1, 4)
+    sample = (f"torch CPU FP32 alpha*(A@B)+beta*C (the reference tests' check formula) on "
+              f"{rows} of {m} rows per call, K={k}, N={n}, 2 warm-up calls")
+    summary = {k_: {"ours_device_us": v.get("device_us"), "cublas_device_us": v.get("cublas_device_us"),
+                    "ours_cold_us": v.get("cold_us"), "cublas_cold_us": v.get("cublas_cold_us"),
+                    "vs_cublas_device": v.get("vs_cublas_device")}
+               for k_, v in configs.items()}
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": 1,
         "steps": steps, "warmup": warmup, "warmup_steps_run": warm_run,
         "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp16 in, fp32 accumulate",
         "data": "synthetic (seeded on device: A,B ~ N(0,1/sqrt(K)), C ~ U[-1,1))",
-        "config": {"workload": "square FP16 GEMM M=N=K=8192, alpha=1, beta=0.5 (BASELINE configs[1])",
-                   "M": m, "N": n, "K": k, "alpha": alpha, "beta": beta, "parallelism": "1 GPU",
-                   "l2": "inputs (384 MiB) larger than the 126 MB L2; no flush"},
+        "config": workload_config(1, cfgs),
+        "device": "1 B200 (this library, gemm_launcher_stream)",
         "roofline": roof,
-        "cublas": {"tflops": round(flops / ms_cub / 1e9, 2), "ms": round(ms_cub, 4),
-                   "ours_tflops_paired": round(flops / ms_pair / 1e9, 2),
-                   "ours_vs_cublas": round(ms_cub / ms_pair, 4),
-                   "method": "median of 5 alternating blocks of `steps` calls each, both warm"},
         "e2e": {"value": round(flops / e2e_ms / 1e9, 3), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "api": "gemm_b200.gemm_host (slab-pipelined H2D / gemm_launcher / D2H on three "
                        "streams), pinned host buffers"},
-        "cpu_baseline": {"value": round(tflops_cpu, 4), "unit": "TFLOP/s", "cores": threads,
-                         "kind": "port",
-                         "sample": f"torch CPU FP32 alpha*(A@B)+beta*C on {rows} of {m} rows "
-                                   f"(K={k}, N={n}), {secs:.1f} s"},
+        "cpu_baseline": {"value": round(tf_all, 4), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port", "sample": sample + f", {cpu_steps} timed calls"},
+        "cpu_baseline_4threads": {"value": round(tf_4, 4), "unit": "TFLOP/s", "cores": 4,
+                                  "kind": "port",
+                                  "sample": sample + ", 1 timed call (the reference test pins 4 "
+                                                     "threads, tests/test_gemm.py:189)"},
         "gpu_launches": steps,
-        "clocks": clk.summary(),
         "configs": configs,
+        "clocks": clk.summary(),
+        "small_configs": summary,
+        "cublas": {"tflops": round(flops / ms_cub / 1e9, 2), "ms": round(ms_cub, 4),
+                   "ours_tflops_paired": round(flops / ms_pair / 1e9, 2),
+                   "ours_vs_cublas": round(ms_cub / ms_pair, 4),
+                   "method": "8192^3: median of 5 alternating blocks of `steps` calls, both warm"},
     }
     return out
 
 
 # ---------------------------------------------------------------------------
-# multi-GPU slab workload (weak scaling)
+# multi-GPU slab workload (weak scaling, plus the fixed problem)
 # ---------------------------------------------------------------------------
-def run_multi(args, gb, oracle_cfgs, device, pk, rank, world):
+def verify_rank(sets, b_dev, alpha, rank, world, rows=256, spots=64):
+    """Check this rank's results against the CPU oracle (beta == 0 results:
+    C = alpha * A @ B). For every (name, a_dev, c_dev) in `sets`: a seeded
+    sample of `rows` rows against the oracle's FP32 formula (both tolerance
+    rules) and `spots` single elements against its FP64 audit. Returns a dict
+    of per-set figures (pass flag, worst scaled error, relative Frobenius
+    error, worst FP64 spot error)."""
+    sys.path.insert(0, str(REPO))
+    from oracle import oracle
+    torch.set_num_threads(max(1, oracle.cpu_threads() // max(world, 1)))
+    g = torch.Generator().manual_seed(1000 + rank)
+    b_h = b_dev.cpu()
+    picked = []
+    for name, a_d, c_d in sets:
+        idx = torch.randperm(a_d.shape[0], generator=g)[:rows].sort().values
+        idx_d = idx.to(a_d.device)
+        picked.append((name, a_d[idx_d].cpu(), c_d[idx_d].cpu()))
+    a_cat = torch.cat([p[1] for p in picked])
+    ref = oracle.reference_fp32(a_cat, b_h, None, alpha, 0.0)
+    out, r0 = {}, 0
+    n = b_h.shape[1]
+    for name, a_rows, c_rows in picked:
+        rr = a_rows.shape[0]
+        chk = oracle.check(c_rows, ref[r0:r0 + rr])
+        r0 += rr
+        si = torch.randint(0, rr, (spots,), generator=g)
+        sj = torch.randint(0, n, (spots,), generator=g)
+        zeros = torch.zeros((rr, n), dtype=torch.float16)
+        f64 = oracle.audit_f64(a_rows, b_h, zeros, alpha, 0.0, si.numpy(), sj.numpy())
+        got = c_rows[si, sj].double().numpy()
+        err = abs(got - f64)
+        spot_scaled = float((err / (1.0 + abs(f64))).max())
+        spot_ok = bool((err <= oracle.REF_ATOL + oracle.REF_RTOL * abs(f64)).all()
+                       and spot_scaled <= oracle.NS_ABS)
+        out[name] = {"pass": bool(chk.passed and spot_ok), "max_scaled": chk.max_scaled_error,
+                     "rel_frob": chk.rel_frobenius, "fp64_spot_max_scaled": spot_scaled}
+    return out
+
+
+def run_multi(args, gb, cfgs, device, pk, rank, world):
     import torch.distributed as dist
-    cfg = oracle_cfgs["sharded32768"]
+    from gemm_b200.slab import SlabGemm
+    cfg = cfgs["sharded32768"]
     slab_m = cfg["m"] // 8  # 4096 rows per rank: the 8-GPU partition of the config
     m_total = slab_m * world
     n, k, alpha, beta = cfg["n"], cfg["k"], cfg["alpha"], cfg["beta"]
     stream = torch.cuda.current_stream()
+
+    def max_over_ranks(x, op=dist.ReduceOp.MAX):
+        t = torch.tensor([float(x)], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=op)
+        return float(t.item())
+
     # B from rank 0, broadcast once over NCCL (timed on the device, max over ranks)
     if rank == 0:
         g = torch.Generator(device=device).manual_seed(0)
@@ -419,86 +600,135 @@ def run_multi(args, gb, oracle_cfgs, device, pk, rank, world):
         dist.broadcast(b, src=0)
         ev1.record(stream)
         torch.cuda.synchronize()
-        t = torch.tensor([ev0.elapsed_time(ev1)], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        bcast_times.append(float(t.item()))
-    bcast_ms = torch.tensor([min(bcast_times)], device=device)
+        bcast_times.append(max_over_ranks(ev0.elapsed_time(ev1)))
+    bcast_ms = min(bcast_times)
     del warm
+    # every rank holds the same B: a position-weighted checksum of its bits
+    bits = b.view(torch.int16)
+    row_w = torch.arange(1, k + 1, device=device, dtype=torch.float64)
+    col_w = torch.arange(1, n + 1, device=device, dtype=torch.float64)
+    csum = [float((bits.sum(dim=1, dtype=torch.int64).double() * row_w).sum().item()),
+            float((bits.sum(dim=0, dtype=torch.int64).double() * col_w).sum().item())]
+    b_same = all(max_over_ranks(x) == max_over_ranks(x, dist.ReduceOp.MIN) for x in csum)
+    del bits, row_w, col_w
     # this rank's A slab (seed = rank) and C slab (zero)
     g = torch.Generator(device=device).manual_seed(1 + rank)
     a = (torch.randn((slab_m, k), generator=g, device=device) / math.sqrt(k)).half()
     c = torch.zeros((slab_m, n), device=device, dtype=torch.float16)
+    step = lambda: gb.gemm(a, b, c, alpha, beta)  # noqa: E731
     warmup = max(args.warmup, 3)
-    # at least `warmup` steps and one second per rank (no collective inside)
-    warm_run = warm_up(lambda: gb.gemm(a, b, c, alpha, beta, stream), warmup, 1.0)
+    # the same slab on one GPU alone (rank 0; the others wait): per-GPU reference of this run
     dist.barrier()
+    alone_ms = 0.0
+    if rank == 0:
+        warm_up(step, warmup, 1.0)
+        alone_ms = time_block(step, args.steps)
+    alone_ms = max_over_ranks(alone_ms)
+    # at least `warmup` steps and one second per rank (no collective inside)
+    warm_run = warm_up(step, warmup, 1.0)
+    dist.barrier()
+    torch.cuda.synchronize()
+    dist.barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
     with ClockSampler(device) as clk:
-        torch.cuda.synchronize()
-        dist.barrier()
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for _ in range(args.steps):
-            gb.gemm(a, b, c, alpha, beta, stream)
+            step()
         end.record(stream)
         torch.cuda.synchronize()
-        dist.barrier()
-        time.sleep(0.25)
-    ms = torch.tensor([start.elapsed_time(end) / args.steps], device=device)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    dist.barrier()
+    ms_v = max_over_ranks(start.elapsed_time(end) / args.steps)
     st = gb.status()
     if st != 0:
         raise RuntimeError(f"rank {rank}: library status {st}")
-    ms_v = float(ms.item())
     flops_total = 2.0 * m_total * n * k
     value = flops_total / ms_v / 1e9
-    # e2e per rank: this rank's A slab and C slab cross PCIe each step (B stays resident:
-    # it is replicated once by the broadcast, per the config)
-    a_h, c_h = a.cpu().pin_memory(), c.cpu().pin_memory()
+    c_plain = c.clone()  # beta = 0: every step leaves C = A @ B
+
+    # e2e per rank through gemm_host: this rank's A slab crosses PCIe every step
+    # and its C slab comes back (beta = 0: C is not read, so not sent); B stays
+    # resident (replicated once by the broadcast, per the config)
+    a_h = a.cpu().pin_memory()
+    c_h = torch.zeros((slab_m, n), dtype=torch.float16).pin_memory()
     c_out = torch.empty_like(c_h).pin_memory()
-    a_d, c_d = torch.empty_like(a), torch.empty_like(c)
 
     def e2e_step():
-        a_d.copy_(a_h, non_blocking=True)
-        c_d.copy_(c_h, non_blocking=True)
-        gb.gemm(a_d, b, c_d, alpha, beta, stream)
-        c_out.copy_(c_d, non_blocking=True)
+        gb.gemm_host(a_h, b, c_h, alpha, beta, out=c_out, stream=stream)
 
     dist.barrier()
-    e2e = torch.tensor([time_calls(e2e_step, 3, 1, stream)], device=device)
-    dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
-    e2e_ms = float(e2e.item())
+    warm_up(e2e_step, 1, 0.0)
+    e2e_ms = max_over_ranks(time_block(e2e_step, 3))
+    e2e_ok = max_over_ranks(1.0 if torch.equal(c_out, c_plain.cpu()) else 0.0, dist.ReduceOp.MIN)
+    h2d_rank = a.numel() * 2 + (c.numel() * 2 if beta != 0 else 0)
+
     # B's broadcast overlapped with the GEMM (SlabGemm.broadcast_and_run: B's
     # column blocks consumed as they land), against broadcast-then-GEMM.
-    from gemm_b200.slab import SlabGemm
-    c_plain = c.clone()  # beta = 0: every step leaves C = A @ B
     bgroup = SlabGemm.broadcast_group(list(range(world)), args.bcast_reserve_sms)
     sg = SlabGemm(bcast_group=bgroup)
     warm_b = torch.zeros(16 << 20, device=device, dtype=torch.float16)
     dist.broadcast(warm_b, src=0, group=bgroup)  # communicator set-up outside the timing
     torch.cuda.synchronize()
     del warm_b
-    ov_times = []
-    for _ in range(3):
-        dist.barrier()
-        torch.cuda.synchronize()
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ev0.record(stream)
-        blocks = sg.broadcast_and_run(a, b, c, alpha, beta, src=0, chunks=args.bcast_chunks,
-                                      reserve_sms=args.bcast_reserve_sms)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        t = torch.tensor([ev0.elapsed_time(ev1)], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ov_times.append(float(t.item()))
-        del blocks
-    same = torch.tensor([1 if torch.equal(c, c_plain) else 0], device=device)
-    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+
+    def overlapped(a_s, c_s, reps):
+        times = []
+        for _ in range(reps):
+            dist.barrier()
+            torch.cuda.synchronize()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+            blocks = sg.broadcast_and_run(a_s, b, c_s, alpha, beta, src=0,
+                                          chunks=args.bcast_chunks,
+                                          reserve_sms=args.bcast_reserve_sms)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            times.append(max_over_ranks(ev0.elapsed_time(ev1)))
+            del blocks
+        return min(times)
+
+    c_ov = torch.empty_like(c)
+    ov_ms = overlapped(a, c_ov, 3)
+    same = max_over_ranks(1.0 if torch.equal(c_ov, c_plain) else 0.0, dist.ReduceOp.MIN)
+
+    # strong scaling: the fixed 32768-row problem on `world` GPUs (this rank's
+    # share of the rows, broadcast of B overlapped), against the whole problem
+    # on one GPU (rank 0 alone, B already resident: nothing to broadcast)
+    m_fix = cfg["m"]
+    _, rows_fix = gb.slab_rows(m_fix, world, rank)
+    g = torch.Generator(device=device).manual_seed(100 + rank)
+    a_fix = (torch.randn((rows_fix, k), generator=g, device=device) / math.sqrt(k)).half()
+    c_fix = torch.zeros((rows_fix, n), device=device, dtype=torch.float16)
+    overlapped(a_fix, c_fix, 1)  # warm-up at this size
+    strong_ms = overlapped(a_fix, c_fix, 2)
+    dist.barrier()
+    t1_ms = 0.0
+    if rank == 0:
+        g = torch.Generator(device=device).manual_seed(7)
+        a_all = (torch.randn((m_fix, k), generator=g, device=device) / math.sqrt(k)).half()
+        c_all = torch.zeros((m_fix, n), device=device, dtype=torch.float16)
+        one = lambda: gb.gemm(a_all, b, c_all, alpha, beta)  # noqa: E731
+        warm_up(one, 2, 1.0)
+        t1_ms = time_block(one, 3)
+        del a_all, c_all
+    t1_ms = max_over_ranks(t1_ms)
     dist.destroy_process_group(bgroup)
     st = gb.status()
     if st != 0:
         raise RuntimeError(f"rank {rank}: library status {st} in the overlapped broadcast")
+
+    # every rank's results against the CPU oracle (outside every timed region)
+    ver = verify_rank([("steps", a, c_plain), ("overlapped_broadcast", a, c_ov),
+                       ("strong_scaling", a_fix, c_fix)], b, alpha, rank, world)
+    ver_all = {}
+    for name, v in ver.items():
+        ver_all[name] = {"pass": bool(max_over_ranks(1.0 if v["pass"] else 0.0, dist.ReduceOp.MIN)),
+                         "max_scaled": max_over_ranks(v["max_scaled"]),
+                         "rel_frob": max_over_ranks(v["rel_frob"]),
+                         "fp64_spot_max_scaled": max_over_ranks(v["fp64_spot_max_scaled"])}
+    verified = all(v["pass"] for v in ver_all.values()) and b_same
     per_gpu = value / world
+    alone_tflops = 2.0 * slab_m * n * k / alone_ms / 1e9
     if rank != 0:
         return None
     return {
@@ -508,32 +738,40 @@ def run_multi(args, gb, oracle_cfgs, device, pk, rank, world):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "fp16 in, fp32 accumulate",
         "data": "synthetic (seeded on device: A,B ~ N(0,1/sqrt(K)), C = 0)",
-        "config": {"workload": "sharded FP16 GEMM, 4096-row C slab per rank of the "
-                               "32768x32768x16384 config (BASELINE configs[4]); M = 4096 x n_gpus",
-                   "M": m_total, "N": n, "K": k, "alpha": alpha, "beta": beta,
-                   "parallelism": f"C row slabs x{world}, B broadcast once (NCCL)",
-                   "l2": "inputs larger than the 126 MB L2; no flush"},
+        "config": workload_config(world, cfgs),
+        "device": f"{world} B200 (this library), one process per GPU, NCCL",
         "roofline": {"bound": "tensor", "achieved": round(per_gpu, 2), "peak": pk["tflops"],
-                     "unit": "TFLOP/s", "frac": per_gpu / pk["tflops"],
+                     "unit": "TFLOP/s", "frac": round(per_gpu / pk["tflops"], 4),
                      "traffic": traffic_from_profile("tc_gemm_8192"),
                      "peak_source": f"{pk['source']} cuBLAS bf16 burst, per GPU"},
-        "broadcast": {"bytes": k * n * 2, "ms_max_over_ranks": round(float(bcast_ms.item()), 3),
-                      "gbs": round(k * n * 2 / float(bcast_ms.item()) / 1e6, 1),
-                      "note": "one-time replication of B (NCCL over NVLink), best of 3 after a "
-                              "warm-up collective; not inside a step",
-                      "overlapped_with_gemm": {
-                          "ms_max_over_ranks": round(min(ov_times), 3),
-                          "sequential_ms": round(float(bcast_ms.item()) + ms_v, 3),
-                          "chunks": args.bcast_chunks, "reserve_sms": args.bcast_reserve_sms,
-                          "nccl_max_ctas": args.bcast_reserve_sms,
-                          "c_identical_to_plain_path": bool(same.item()),
-                          "method": "B in column blocks, each block's GEMM waits only for that "
-                                    "block; best of 3"}},
         "e2e": {"value": round(flops_total / e2e_ms / 1e9, 3), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3),
-                "h2d_bytes_per_step": (a.numel() + c.numel()) * 2 * world,
-                "d2h_bytes_per_step": c.numel() * 2 * world},
+                "h2d_bytes_per_step": h2d_rank * world,
+                "d2h_bytes_per_step": c.numel() * 2 * world,
+                "c_equal_to_device_steps": bool(e2e_ok),
+                "api": "gemm_b200.gemm_host per rank (A slab in, C slab out, slab-pipelined; "
+                       "B resident after the one-time broadcast)"},
         "gpu_launches": args.steps * world,
+        "verified": bool(verified),
+        "verification": {"rows_per_rank": 256, "fp64_spots_per_rank": 64,
+                         "b_identical_on_all_ranks": bool(b_same), **ver_all},
+        "broadcast": {"bytes": k * n * 2, "ms_max_over_ranks": round(bcast_ms, 3),
+                      "gbs": round(k * n * 2 / bcast_ms / 1e6, 1),
+                      "overlapped_with_gemm": {
+                          "ms_max_over_ranks": round(ov_ms, 3),
+                          "sequential_ms": round(bcast_ms + ms_v, 3),
+                          "chunks": args.bcast_chunks, "reserve_sms": args.bcast_reserve_sms,
+                          "c_identical_to_plain_path": bool(same)}},
+        "scaling_detail": {
+            "slab_alone_ms": round(alone_ms, 4), "slab_alone_tflops": round(alone_tflops, 2),
+            "per_gpu_tflops": round(per_gpu, 2),
+            "per_gpu_efficiency": round(per_gpu / alone_tflops, 4),
+            "note": "per_gpu_efficiency = (value / n_gpus) / the same 4096-row slab timed on "
+                    "rank 0 alone in this run; the N=1 bench line is the 8192^3 config, a "
+                    "different workload",
+            "strong": {"problem": f"{m_fix}x{n}x{k}", "one_gpu_ms": round(t1_ms, 3),
+                       "n_gpu_ms_with_broadcast": round(strong_ms, 3),
+                       "efficiency": round(t1_ms / (world * strong_ms), 4)}},
         "clocks": clk.summary(),
     }
 
@@ -541,50 +779,24 @@ def run_multi(args, gb, oracle_cfgs, device, pk, rank, world):
 # ---------------------------------------------------------------------------
 # reference arm: the reference's CPU check path on the host cores
 # ---------------------------------------------------------------------------
-def run_reference(args, oracle_cfgs, rank, world):
+def run_reference(args, cfgs, rank, world):
     if rank != 0:
         return None
-    sys.path.insert(0, str(REPO))
-    from oracle import oracle
-    if world > 1:
-        cfg = dict(oracle_cfgs["sharded32768"])
-        workload = ("sharded FP16 GEMM, 4096-row C slab per rank of the 32768x32768x16384 config; "
-                    "M = 4096 x n_gpus")
-        m = 4096 * world
-    else:
-        cfg = oracle_cfgs["square8192"]
-        workload = "square FP16 GEMM M=N=K=8192, alpha=1, beta=0.5 (BASELINE configs[1])"
-        m = cfg["m"]
-    n, k, alpha, beta = cfg["n"], cfg["k"], cfg["alpha"], cfg["beta"]
-    threads = oracle.cpu_threads()
-    torch.set_num_threads(threads)
-    # rows per step: a bounded sample so the whole run ends within minutes
-    rows = 64
-    a, b, c = oracle.make_inputs(rows, n, k, cfg["dist"], seed=0)
-    oracle.reference_fp32(a, b, c, alpha, beta)
-    t0 = time.perf_counter()
-    oracle.reference_fp32(a, b, c, alpha, beta)
-    dt = max(time.perf_counter() - t0, 1e-6)
-    per_step_budget = max(0.5, min(10.0, 60.0 / max(args.steps + args.warmup, 1)))
-    rows = int(max(64, min(m, rows * per_step_budget / dt)))
-    a, b, c = oracle.make_inputs(rows, n, k, cfg["dist"], seed=0)
-    for _ in range(max(args.warmup, 1)):
-        oracle.reference_fp32(a, b, c, alpha, beta)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        oracle.reference_fp32(a, b, c, alpha, beta)
-    secs = time.perf_counter() - t0
-    ms = secs / args.steps * 1e3
-    value = 2.0 * rows * n * k / (ms * 1e-3) / 1e12
+    config = workload_config(world, cfgs)
+    cfg = cfgs["sharded32768"] if world > 1 else cfgs["square8192"]
+    m, n, k, alpha, beta = config["M"], config["N"], config["K"], cfg["alpha"], cfg["beta"]
+    threads = cpu_threads()
+    value, ms, rows = cpu_formula_rate(m, n, k, cfg["dist"], alpha, beta, CPU_SAMPLE_ROWS,
+                                       args.steps, max(args.warmup, 2), threads)
     sample = (f"torch CPU FP32 alpha*(A@B)+beta*C (the reference tests' check formula) on {rows} "
-              f"of {m} rows per step, K={k}, N={n}")
+              f"of {m} rows per call, K={k}, N={n}, {max(args.warmup, 2)} warm-up calls")
     return {
         "metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "fp16 in, fp32 accumulate (CPU)", "data": "synthetic (seeded CPU generator)",
-        "config": {"workload": workload, "M": m, "N": n, "K": k, "alpha": alpha, "beta": beta,
-                   "parallelism": "host CPU cores"},
+        "config": config,
+        "device": f"host CPU, {threads} threads",
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -603,12 +815,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--quick", action="store_true", help="skip the secondary configs")
-    ap.add_argument("--cpu-budget", type=float, default=8.0, help="seconds of CPU baseline work")
     ap.add_argument("--only", default=None,
                     help="time one config of oracle.CONFIGS (ours and cuBLAS) and exit")
     ap.add_argument("--tn", action="store_true", help="with --only: time gemm_launcher_tn")
     ap.add_argument("--shape", default=None,
                     help="with --only: override M,N,K of the config (e.g. 2048,2048,8192)")
+    ap.add_argument("--cold", action="store_true", help="with --only: add the cold-L2 times")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -636,8 +848,8 @@ def main():
             cfg["m"] = 4096
         if args.shape:
             cfg["m"], cfg["n"], cfg["k"] = (int(x) for x in args.shape.split(","))
-        r = measure_config(gb, args.only, cfg, torch.cuda.current_stream(), args.steps,
-                           args.warmup, device, tn=args.tn)
+        r = measure_config(gb, args.only, cfg, args.steps, args.warmup, device,
+                           flush=L2Flush(device) if args.cold else None, tn=args.tn)
         print(json.dumps({"only": args.only, **r}), flush=True)
         return
     if world > 1:

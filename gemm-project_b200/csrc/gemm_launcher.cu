@@ -75,7 +75,7 @@ struct DeviceInfo {
   int split_clusters[3] = {0, 0, 0};   // co-resident (1, ks) split-K clusters, ks = 2, 4, 8
   int* err = nullptr;
   cudaMemPool_t pool = nullptr;   // repack scratch (never trimmed between calls)
-  bool configured = false;
+  std::atomic<bool> configured{false};
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mutex;
@@ -129,6 +129,14 @@ void configure_tc() {
   cudaFuncSetAttribute(tc_gemm_kernel<BN, PAIR, true, SLABS, SLAB_N>,
                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                        TcCfg<BN, PAIR, true, SLABS, SLAB_N>::kSmemBytes);
+  if constexpr (!PAIR && SLABS == 1 && !SLAB_N) {
+    cudaFuncSetAttribute(tc_gemm_kernel<BN, false, false, 1, false, true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         TcCfg<BN, false, false, 1, false, true>::kSmemBytes);
+    cudaFuncSetAttribute(tc_gemm_kernel<BN, false, true, 1, false, true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         TcCfg<BN, false, true, 1, false, true>::kSmemBytes);
+  }
 }
 
 // Co-resident 2-CTA clusters of a pair kernel (0 if it cannot be placed).
@@ -197,9 +205,9 @@ DeviceInfo& device_info() {
   int dev = 0;
   cudaGetDevice(&dev);
   DeviceInfo& d = g_dev[dev % kMaxDevices];
-  if (d.configured) return d;
+  if (d.configured.load(std::memory_order_acquire)) return d;
   std::lock_guard<std::mutex> lock(g_dev_mutex);
-  if (!d.configured) {
+  if (!d.configured.load(std::memory_order_relaxed)) {
     cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     void* p = nullptr;
     record_error(cudaGetSymbolAddress(&p, g_device_error));
@@ -285,8 +293,7 @@ DeviceInfo& device_info() {
                    d.stream_slots, d.dec_slots[0], d.dec_slots[1], d.dec_slots[2],
                    d.split_clusters[0], d.split_clusters[1], d.split_clusters[2]);
     }
-    std::atomic_thread_fence(std::memory_order_release);
-    d.configured = true;
+    d.configured.store(true, std::memory_order_release);
   }
   return d;
 }
@@ -465,11 +472,11 @@ int raster_group(int tiles_m, int tiles_n) {
 // first global-memory access (griddepcontrol.wait). GEMM_PDL=0 turns it off.
 bool pdl_enabled() { return env_int_default("GEMM_PDL", 1) != 0; }
 
-template <int BN, bool PAIR, bool BKM, int SLABS, bool SLAB_N = false>
+template <int BN, bool PAIR, bool BKM, int SLABS, bool SLAB_N = false, bool LSU = false>
 void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                   const TcParams& p, const DeviceInfo& d, cudaStream_t s, int M, int N, int K,
                   int max_sms) {
-  using Cfg = TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>;
+  using Cfg = TcCfg<BN, PAIR, BKM, SLABS, SLAB_N, LSU>;
   const int tiles = p.tiles_m * p.tiles_n;
   static const char* names[2][6] = {
       {"tc_gemm_kernel<128x64>", "tc_gemm_kernel<128x128>", "tc_gemm_kernel<128x256>",
@@ -478,9 +485,13 @@ void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
       {"tc_gemm_kernel<128x64,tn>", "tc_gemm_kernel<128x128,tn>", "tc_gemm_kernel<128x256,tn>",
        "tc_gemm_kernel<256x256,pair,tn>", "tc_gemm_kernel<512x256,pair,tn>",
        "tc_gemm_kernel<256x512,pair,tn>"}};
+  static const char* lsu_names[2][3] = {
+      {"tc_gemm_kernel<128x64,lsu>", "tc_gemm_kernel<128x128,lsu>", "tc_gemm_kernel<128x256,lsu>"},
+      {"tc_gemm_kernel<128x64,tn,lsu>", "tc_gemm_kernel<128x128,tn,lsu>",
+       "tc_gemm_kernel<128x256,tn,lsu>"}};
   const int idx =
       PAIR ? (SLAB_N ? 5 : (SLABS == 2 ? 4 : 3)) : (BN == 64 ? 0 : (BN == 128 ? 1 : 2));
-  const char* name = names[BKM ? 1 : 0][idx];
+  const char* name = LSU ? lsu_names[BKM ? 1 : 0][idx < 3 ? idx : 0] : names[BKM ? 1 : 0][idx];
   cudaLaunchConfig_t cfg{};
   cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
@@ -516,26 +527,33 @@ void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   cfg.attrs = attr;
   cfg.numAttrs = na;
   log_launch(name, M, N, K, cfg.gridDim, cfg.blockDim);
-  record_error(cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, PAIR, BKM, SLABS, SLAB_N>, ta, tb, tc, p));
+  record_error(
+      cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, PAIR, BKM, SLABS, SLAB_N, LSU>, ta, tb, tc, p));
 }
 
 // Encode the tensor maps and launch the tcgen05 kernel for `tile` on operands
 // that are TMA-addressable as given (pitches lda/ldb in elements).
 // b_kmajor: B is given as Bt[N,K] (row pitch ldb), i.e. C = A * Bt^T.
+// lsu: A and B are read with per-thread loads (any alignment and pitch, no
+// tensor maps); single-CTA tiles (64, 128, 256) only.
 int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half* C, int M, int N,
                    int K, float alpha, float beta, cudaStream_t s, int tile, const DeviceInfo& d,
-                   bool b_kmajor = false, int ldc = 0, int max_sms = 0, int ksplit = 1) {
+                   bool b_kmajor = false, int ldc = 0, int max_sms = 0, int ksplit = 1,
+                   bool lsu = false) {
   if (ldc <= 0) ldc = N;
+  if (lsu && tile != 64 && tile != 128 && tile != 256) tile = 256;
   const bool pair = tile == kTilePair || tile == kTilePair2 || tile == kTilePairN;
   const int slabs = tile == kTilePair2 ? 2 : 1;  // A slabs per CTA
   CUtensorMap ta, tb, tc;
+  std::memset(&ta, 0, sizeof(ta));
+  std::memset(&tb, 0, sizeof(tb));
   std::memset(&tc, 0, sizeof(tc));
   const uint32_t b_rows = pair ? 128u : static_cast<uint32_t>(tile);
-  const bool ok_b = b_kmajor
-                        ? make_tmap(&tb, b_src, K, N, static_cast<uint64_t>(ldb) * 2, 64, b_rows)
-                        : make_tmap(&tb, b_src, N, K, static_cast<uint64_t>(ldb) * 2, 64, 64);
+  const bool ok_b =
+      lsu || (b_kmajor ? make_tmap(&tb, b_src, K, N, static_cast<uint64_t>(ldb) * 2, 64, b_rows)
+                       : make_tmap(&tb, b_src, N, K, static_cast<uint64_t>(ldb) * 2, 64, 64));
   const bool ok_a =
-      make_tmap(&ta, a_src, K, M, static_cast<uint64_t>(lda) * 2, 64, 128u * slabs);
+      lsu || make_tmap(&ta, a_src, K, M, static_cast<uint64_t>(lda) * 2, 64, 128u * slabs);
   // C goes through TMA (32 x 32 boxes, 64B swizzle) when it is TMA-addressable.
   const int c_tma = aligned16(C) && ldc % 8 == 0 &&
                     make_tmap(&tc, C, N, M, static_cast<uint64_t>(ldc) * 2, 32, 32,
@@ -569,6 +587,26 @@ int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half*
   if (ksplit > 1 && !pair) {
     p.ksplit = ksplit;
     p.kb_per = ceil_div(p.num_kb, ksplit);
+  }
+  p.A = a_src;
+  p.B = b_src;
+  p.lda = lda;
+  p.ldb = ldb;
+  if (lsu) {
+    if (b_kmajor) {
+      switch (tile) {
+        case 64: launch_tc_bn<64, false, true, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+        case 128: launch_tc_bn<128, false, true, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+        default: launch_tc_bn<256, false, true, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+      }
+    } else {
+      switch (tile) {
+        case 64: launch_tc_bn<64, false, false, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+        case 128: launch_tc_bn<128, false, false, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+        default: launch_tc_bn<256, false, false, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
+      }
+    }
+    return 0;
   }
   if (b_kmajor) {
     switch (tile) {
@@ -639,8 +677,55 @@ void repack_operands(const half* A, const half* B, int M, int N, int K, cudaStre
   }
 }
 
-int launch_tc(const half* A, const half* B, half* C, int M, int N, int K, float alpha, float beta,
-              cudaStream_t s, int tile, const DeviceInfo& d) {
+// Operands the tcgen05 path cannot read through TMA (a base that is not
+// 16-byte aligned, or a row pitch that is not a multiple of 16 bytes: K % 8 or
+// N % 8 != 0, the reference's misaligned cases).
+bool a_tma_ok(const half* A, int K) { return aligned16(A) && K % 8 == 0; }
+bool b_tma_ok(const half* B, int N) { return aligned16(B) && N % 8 == 0; }
+
+// Such operands are read in place by the LSU variant of the tile kernel (per-
+// thread loads into the same swizzled stages: no repack pass, no scratch), up
+// to a problem size where its slower operand feed would cost more than a
+// repack pass over A and B plus the TMA-fed kernel (measured on B200; beyond
+// it the repack path runs). GEMM_LSU=1 forces the LSU variant, -1 the repack.
+constexpr double kLsuMaxFlops = 3.5e10;
+
+bool use_lsu(int M, int N, int K) {
+  const int f = env_int("GEMM_LSU");
+  if (f != 0) return f > 0;
+  return 2.0 * M * N * K <= kLsuMaxFlops;
+}
+
+// Tile choice among the single-CTA tiles (those the LSU variant has).
+int choose_tile_single(int M, int N, const DeviceInfo& d) {
+  const int forced = env_int("GEMM_TILE");
+  if (forced == 64 || forced == 128 || forced == 256) return forced;
+  int best = 256;
+  float best_cost = 1e30f;
+  for (const int bn : {256, 128, 64}) {
+    const long tiles = static_cast<long>(ceil_div(M, 128)) * ceil_div(N, bn);
+    const long waves = (tiles + d.sms - 1) / d.sms;
+    const float eff = bn == 256 ? 0.95f : (bn == 128 ? 0.8f : 0.6f);
+    const float cost = static_cast<float>(waves) * bn / eff;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+// How the tcgen05 path runs a call: tile code, K split, and whether A and B
+// are read in place by the LSU variant or repacked into scratch.
+struct TcPlan {
+  int tile;
+  int ksplit;
+  bool lsu;
+  bool repack;  // scratch needed (repack_bytes() of the operands)
+};
+
+TcPlan plan_tc(const half* A, const half* B, int M, int N, int K, int tile, const DeviceInfo& d,
+               bool force_lsu) {
   int ksplit = 1;
   if (tile == 0 || tile == kTileSplitK) {
     const SplitPlan plan = split_k_plan(M, N, K, d);
@@ -655,28 +740,54 @@ int launch_tc(const half* A, const half* B, half* C, int M, int N, int K, float 
     }
   }
   if (tile != 0 && !tile_available(tile, d)) tile = 256;
-  if (tile == 0) tile = choose_tile(M, N, d);
-  const size_t need = repack_bytes(A, B, M, N, K);
+  const bool aligned = a_tma_ok(A, K) && b_tma_ok(B, N);
+  const bool lsu = force_lsu || (!aligned && use_lsu(M, N, K));
+  if (tile == 0) tile = lsu ? choose_tile_single(M, N, d) : choose_tile(M, N, d);
+  if (lsu && tile != 64 && tile != 128) tile = 256;  // single-CTA tiles only
+  return TcPlan{tile, ksplit, lsu, !lsu && !aligned};
+}
+
+// Run a plan. Repack scratch comes from `scratch` when given (the no-alloc
+// entry point's fixed buffer), else stream-ordered from this library's pool.
+int launch_tc_planned(const half* A, const half* B, half* C, int M, int N, int K, float alpha,
+                      float beta, cudaStream_t s, const TcPlan& plan, const DeviceInfo& d,
+                      void* scratch = nullptr) {
+  if (plan.lsu)
+    return launch_tc_core(A, K, B, N, C, M, N, K, alpha, beta, s, plan.tile, d,
+                          /*b_kmajor=*/false, /*ldc=*/0, /*max_sms=*/0, plan.ksplit, /*lsu=*/true);
   const half* a_src = A;
   const half* b_src = B;
   int lda = K, ldb = N;
-  void* scratch = nullptr;
-  if (need) {
-    // Stream-ordered scratch from this library's pool (never trimmed between
-    // calls, so steady-state calls reuse the same memory without a sync).
-    const cudaError_t e = d.pool ? cudaMallocFromPoolAsync(&scratch, need, d.pool, s)
-                                 : cudaMallocAsync(&scratch, need, s);
-    if (e != cudaSuccess) {
-      record_error(e);
-      return -1;
+  void* pooled = nullptr;
+  if (plan.repack) {
+    if (scratch == nullptr) {
+      // Stream-ordered scratch from this library's pool (never trimmed between
+      // calls, so steady-state calls reuse the same memory without a sync).
+      const size_t need = repack_bytes(A, B, M, N, K);
+      const cudaError_t e = d.pool ? cudaMallocFromPoolAsync(&pooled, need, d.pool, s)
+                                   : cudaMallocAsync(&pooled, need, s);
+      if (e != cudaSuccess) {
+        record_error(e);
+        return -1;
+      }
+      static const char* const names[2] = {"pack_rows_kernel<A>", "pack_rows_kernel<B>"};
+      repack_operands(A, B, M, N, K, s, d, pooled, names, &a_src, &lda, &b_src, &ldb);
+    } else {
+      static const char* const names[2] = {"pack_rows_kernel<A,static>",
+                                           "pack_rows_kernel<B,static>"};
+      repack_operands(A, B, M, N, K, s, d, scratch, names, &a_src, &lda, &b_src, &ldb);
     }
-    static const char* const names[2] = {"pack_rows_kernel<A>", "pack_rows_kernel<B>"};
-    repack_operands(A, B, M, N, K, s, d, scratch, names, &a_src, &lda, &b_src, &ldb);
   }
-  const int rc = launch_tc_core(a_src, lda, b_src, ldb, C, M, N, K, alpha, beta, s, tile, d,
-                                /*b_kmajor=*/false, /*ldc=*/0, /*max_sms=*/0, ksplit);
-  if (scratch) cudaFreeAsync(scratch, s);
+  const int rc = launch_tc_core(a_src, lda, b_src, ldb, C, M, N, K, alpha, beta, s, plan.tile, d,
+                                /*b_kmajor=*/false, /*ldc=*/0, /*max_sms=*/0, plan.ksplit);
+  if (pooled) cudaFreeAsync(pooled, s);
   return rc;
+}
+
+int launch_tc(const half* A, const half* B, half* C, int M, int N, int K, float alpha, float beta,
+              cudaStream_t s, int tile, const DeviceInfo& d, bool force_lsu = false) {
+  return launch_tc_planned(A, B, C, M, N, K, alpha, beta, s,
+                           plan_tc(A, B, M, N, K, tile, d, force_lsu), d);
 }
 
 template <int MR, bool VEC, int TPR>
@@ -985,6 +1096,21 @@ int launch_dec(const half* A, const half* B, half* C, int M, int N, int K, float
   return 0;
 }
 
+// The kernel family the automatic dispatch picks (M, N > 0 and K > 0): the
+// `path` codes of gemm_launcher_ex.
+int auto_path(const half* A, const half* B, int M, int N, int K, const DeviceInfo& d) {
+  if (M == 1 || (M == 2 && rows_tma_ok(A, B, M, N, K, d)))
+    return 2;  // streaming GEMV (M = 2: faster than the tensor-core kernel)
+  // 32 < M <= 64: the dense path when its split-K plan applies (few output
+  // tiles), the small-M kernel otherwise
+  if (N > 1 && M <= 64 && dec_ok(A, B, M, N, K, d) &&
+      (M <= 32 || !few_dense_tiles(M, N, d) || split_k_plan(M, N, K, d).ks == 1))
+    return 6;  // small-M tensor-core kernel
+  if (M <= 8) return 2;  // misaligned small M: per-thread loads
+  if (N == 1) return 3;
+  return 1;
+}
+
 int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float alpha, float beta,
              cudaStream_t s, int path, int tile_n) {
   if (M <= 0 || N <= 0) return 0;
@@ -996,21 +1122,10 @@ int dispatch(const half* A, const half* B, half* C, int M, int N, int K, float a
   if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256 && tile_n != kTilePair &&
       tile_n != kTilePair2 && tile_n != kTilePairN && tile_n != kTileSplitK)
     return -1;
-  if (path == 0) {
-    if (M == 1 || (M == 2 && rows_tma_ok(A, B, M, N, K, d)))
-      path = 2;                       // streaming GEMV (M = 2: faster than the tensor-core kernel)
-    else if (N > 1 && M <= 64 && dec_ok(A, B, M, N, K, d) &&
-             (M <= 32 || !few_dense_tiles(M, N, d)))
-      path = 6;                       // small-M tensor-core kernel
-    else if (M <= 8)
-      path = 2;                       // misaligned small M: per-thread loads
-    else if (N == 1)
-      path = 3;
-    else
-      path = 1;
-  }
+  if (path == 0) path = auto_path(A, B, M, N, K, d);
   switch (path) {
     case 1: return launch_tc(A, B, C, M, N, K, alpha, beta, s, tile_n, d);
+    case 7: return launch_tc(A, B, C, M, N, K, alpha, beta, s, tile_n, d, /*force_lsu=*/true);
     case 2:
       if (rows_tma_ok(A, B, M, N, K, d)) return launch_rows_tma(A, B, C, M, N, K, alpha, beta, s, d);
       return launch_rows(A, B, C, M, N, K, alpha, beta, s, d);
@@ -1037,9 +1152,15 @@ int launch_tn(const half* A, const half* Bt, half* C, int M, int N, int K, float
     return 0;
   }
   if (tile != 0 && !tile_available(tile, d)) tile = 256;
-  if (tile == 0) tile = choose_tile(M, N, d);
   const bool a_ok = aligned16(A) && K % 8 == 0;
   const bool b_ok = aligned16(Bt) && K % 8 == 0;
+  if (!(a_ok && b_ok) && use_lsu(M, N, K)) {
+    // read in place by the LSU variant (B K-major): no repack, no scratch
+    if (tile != 64 && tile != 128 && tile != 256) tile = choose_tile_single(M, N, d);
+    return launch_tc_core(A, K, Bt, K, C, M, N, K, alpha, beta, s, tile, d, /*b_kmajor=*/true,
+                          /*ldc=*/0, /*max_sms=*/0, /*ksplit=*/1, /*lsu=*/true);
+  }
+  if (tile == 0) tile = choose_tile(M, N, d);
   size_t a_bytes = a_ok ? 0 : static_cast<size_t>(M) * round_up8(K) * sizeof(half);
   a_bytes = (a_bytes + 255) / 256 * 256;
   const size_t b_bytes = b_ok ? 0 : static_cast<size_t>(N) * round_up8(K) * sizeof(half);
@@ -1101,7 +1222,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 struct NoAllocScratch {
   void* ptr = nullptr;
-  bool ready = false;
+  std::atomic<bool> ready{false};
 };
 NoAllocScratch g_noalloc[kMaxDevices];
 std::mutex g_noalloc_mutex;
@@ -1116,9 +1237,9 @@ void* noalloc_scratch_ptr() {
     return nullptr;
   }
   NoAllocScratch& s = g_noalloc[dev % kMaxDevices];
-  if (s.ready) return s.ptr;
+  if (s.ready.load(std::memory_order_acquire)) return s.ptr;
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!s.ready) {
+  if (!s.ready.load(std::memory_order_relaxed)) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -1126,21 +1247,9 @@ void* noalloc_scratch_ptr() {
       return nullptr;
     }
     s.ptr = p;
-    s.ready = true;
+    s.ready.store(true, std::memory_order_release);
   }
   return s.ptr;
-}
-
-// The repack + tcgen05 path with the fixed scratch buffer (no allocation).
-int launch_tc_static_scratch(const half* A, const half* B, half* C, int M, int N, int K,
-                             float alpha, float beta, cudaStream_t s, const DeviceInfo& d,
-                             void* scratch) {
-  static const char* const names[2] = {"pack_rows_kernel<A,static>", "pack_rows_kernel<B,static>"};
-  const half* a_src;
-  const half* b_src;
-  int lda, ldb;
-  repack_operands(A, B, M, N, K, s, d, scratch, names, &a_src, &lda, &b_src, &ldb);
-  return launch_tc_core(a_src, lda, b_src, ldb, C, M, N, K, alpha, beta, s, choose_tile(M, N, d), d);
 }
 
 }  // namespace
@@ -1226,12 +1335,18 @@ extern "C" GEMM_API int gemm_launcher_tn(const half* A, const half* Bt, half* C,
 extern "C" GEMM_API int gemm_launcher_noalloc(const half* A, const half* B, half* C, int M, int N,
                                               int K, float alpha, float beta, cudaStream_t stream) {
   if (M <= 0 || N <= 0) return 0;
-  const bool tc_path = K > 0 && M > 8 && N != 1;  // the choice dispatch() makes
-  const size_t need = tc_path ? repack_bytes(A, B, M, N, K) : 0;
-  if (need == 0) {
-    // No repack: the kernels dispatch() picks here allocate nothing.
+  DeviceInfo& d = device_info();
+  // The plan gemm_launcher_stream makes for this call (same path, tile and K
+  // split); only where that plan takes repack scratch does this entry point
+  // differ, by taking it from the fixed buffer.
+  TcPlan plan{};
+  const bool tc = K > 0 && auto_path(A, B, M, N, K, d) == 1;
+  if (tc) plan = plan_tc(A, B, M, N, K, 0, d, /*force_lsu=*/false);
+  if (!tc || !plan.repack) {
+    // no repack scratch: the kernels dispatch() picks here allocate nothing
     return dispatch(A, B, C, M, N, K, alpha, beta, stream, 0, 0) == 0 ? 0 : -1;
   }
+  const size_t need = repack_bytes(A, B, M, N, K);
   if (need > kNoAllocScratchBytes) {
     std::fprintf(stderr,
                  "gemm_launcher_noalloc: M=%d N=%d K=%d needs %zu bytes of repack scratch, more "
@@ -1239,10 +1354,9 @@ extern "C" GEMM_API int gemm_launcher_noalloc(const half* A, const half* B, half
                  M, N, K, need, kNoAllocScratchBytes);
     return -2;
   }
-  DeviceInfo& d = device_info();
   void* scratch = noalloc_scratch_ptr();
   if (scratch == nullptr) return -1;
-  return launch_tc_static_scratch(A, B, C, M, N, K, alpha, beta, stream, d, scratch);
+  return launch_tc_planned(A, B, C, M, N, K, alpha, beta, stream, plan, d, scratch);
 }
 
 extern "C" GEMM_API int gemm_selftest_wait_timeout(int timeout_us, cudaStream_t stream) {

@@ -61,10 +61,14 @@
 
 namespace gemm_b200 {
 
-template <int BN_, bool PAIR_, bool BKM_ = false, int SLABS_ = 1, bool SLAB_N_ = false>
+template <int BN_, bool PAIR_, bool BKM_ = false, int SLABS_ = 1, bool SLAB_N_ = false,
+          bool LSU_ = false>
 struct TcCfg {
   static constexpr bool kPair = PAIR_;
   static constexpr bool kBKMajor = BKM_;                // B given as Bt[N,K]
+  // LSU: A and B are loaded by the epilogue warps with per-thread global loads
+  // (any 2-byte alignment, any row pitch) instead of TMA; single-CTA tiles only.
+  static constexpr bool kLsu = LSU_;
   static constexpr int kSlabs = SLABS_;                 // accumulator slabs per CTA
   // Slabs stack along M (two 128-row A slabs sharing the B tile) or, with
   // SLAB_N, along N (two B tiles sharing the A slab: consecutive UMMAs reuse A
@@ -86,7 +90,10 @@ struct TcCfg {
   // cycles per stage with no loads and no UMMAs), so the 128x64, 128x128 and
   // 256x256 pair tiles carry two K blocks per stage: one handshake per eight
   // UMMAs.
-  static constexpr int kKSub = ((!PAIR_ && BN_ <= 128) || (PAIR_ && SLABS_ == 1)) ? 2 : 1;
+  // The LSU variant fills one K block per stage (its loaders hand over each
+  // K block as soon as it is in shared memory).
+  static constexpr int kKSub =
+      LSU_ ? 1 : (((!PAIR_ && BN_ <= 128) || (PAIR_ && SLABS_ == 1)) ? 2 : 1);
   static constexpr int kABlk = kCtaRows * BK * 2;       // A of one K block
   static constexpr int kABytes = kABlk * kKSub;
   // B boxes: N-major B as 64(N) x 64(K) boxes of 8 KiB; K-major B as one box
@@ -137,6 +144,15 @@ struct TcCfg {
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
   static_assert(kTmemCols <= 512, "TMEM columns");
   static_assert(kEpiChunks >= 1, "epilogue chunking");
+  static_assert(!kLsu || (!kPair && kSlabs == 1), "per-thread operand loads: single-CTA tiles");
+  // Per-thread loads: one K block = 128 A rows (K-major) plus BN B columns,
+  // in row segments of 64 halves, 8 lanes (16-byte chunks) per segment.
+  static constexpr int kLsuThreads = 32 * kEpiWarps;
+  static constexpr int kLsuChunksA = 128 * 8;
+  static constexpr int kLsuChunks = kLsuChunksA + BN * 8;
+  static constexpr int kLsuPer = kLsuChunks / kLsuThreads;  // chunks per thread per K block
+  static_assert(kLsuChunks % kLsuThreads == 0 && kLsuChunksA % kLsuThreads == 0,
+                "whole chunks per loader thread");
 };
 
 struct TcParams {
@@ -156,7 +172,94 @@ struct TcParams {
   // partials through distributed shared memory before writing C.
   int ksplit;
   int kb_per;
+  // Operands of the LSU variant (per-thread loads): base pointers at any
+  // 2-byte alignment and row pitches in elements (A[M,K] with pitch lda;
+  // B[K,N], or Bt[N,K] for the TN entry point, with pitch ldb).
+  const half* A;
+  const half* B;
+  long long lda, ldb;
 };
+
+// ---------------------------------------------------------------------------
+// Per-thread operand loads (the LSU variant). A 64-half segment of one row of
+// a row-major FP16 matrix is loaded by 8 lanes, lane c taking the 16-byte chunk
+// of columns [col0 + 8c, col0 + 8c + 8). The row may start at any 2-byte
+// alignment: every lane loads the aligned 16-byte line its chunk starts in, the
+// lane of chunk 7 also the line after, and each lane takes the next line from
+// its neighbour by a shuffle, so the segment costs 8 or 9 aligned loads. Only
+// lines that hold at least one element of the matrix are loaded, so nothing
+// outside the operand's 16-byte lines is touched (allocations are at least
+// 16-byte aligned). Elements outside the matrix read as zero, as TMA's
+// out-of-bounds fill does.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+struct LsuSeg {
+  const uint4* line;  // aligned line holding the segment's first element
+  int phase;          // the first element's position in that line (halves, 0..7)
+  int valid;          // columns of the segment inside the matrix (0..64)
+};
+
+__device__ __forceinline__ LsuSeg lsu_seg(const half* base, long long ld, int rows, int cols, int row,
+                                          int col0) {
+  LsuSeg s;
+  const bool in = row < rows && col0 < cols;
+  s.valid = in ? min(64, cols - col0) : 0;
+  const uintptr_t a0 =
+      reinterpret_cast<uintptr_t>(base + (in ? static_cast<long long>(row) * ld + col0 : 0));
+  s.phase = static_cast<int>((a0 >> 1) & 7u);
+  s.line = reinterpret_cast<const uint4*>(a0 & ~static_cast<uintptr_t>(15));
+  return s;
+}
+
+// Issue this lane's loads of segment `s` (chunk c = lane & 7): its own line and,
+// for chunk 7, the line after it.
+__device__ __forceinline__ void lsu_issue(const LsuSeg& s, int c, uint4& v, uint4& x) {
+  v = make_uint4(0, 0, 0, 0);
+  x = make_uint4(0, 0, 0, 0);
+  if (s.valid > 0 && 8 * c - s.phase < s.valid) v = ldg_nc_v4(s.line + c);
+  if (c == 7 && s.valid > 64 - s.phase) x = ldg_nc_v4(s.line + 8);
+}
+
+// Assemble this lane's chunk from its line and the next one (every lane of the
+// warp must call it: shuffles), zeroing elements outside the matrix.
+__device__ __forceinline__ uint4 lsu_assemble(const LsuSeg& s, int c, const uint4& v, const uint4& x) {
+  uint4 nx;
+  nx.x = __shfl_down_sync(0xffffffffu, v.x, 1, 8);
+  nx.y = __shfl_down_sync(0xffffffffu, v.y, 1, 8);
+  nx.z = __shfl_down_sync(0xffffffffu, v.z, 1, 8);
+  nx.w = __shfl_down_sync(0xffffffffu, v.w, 1, 8);
+  if (c == 7) nx = x;
+  const uint32_t w[8] = {v.x, v.y, v.z, v.w, nx.x, nx.y, nx.z, nx.w};
+  // halves [phase, phase + 8) of the 16 in w: whole words selected by phase / 2
+  // (two select steps), then a half-word shift when the phase is odd
+  const int q = s.phase >> 1;
+  uint32_t t[5];
+#pragma unroll
+  for (int j = 0; j < 5; ++j) {
+    const uint32_t lo = (q & 1) ? w[j + 1] : w[j];
+    const uint32_t hi = (q & 1) ? w[j + 3] : w[j + 2];
+    t[j] = (q & 2) ? hi : lo;
+  }
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) o[j] = (s.phase & 1) ? __byte_perm(t[j], t[j + 1], 0x5432) : t[j];
+  const int vc = s.valid - 8 * c;  // valid elements of this chunk
+  if (vc < 8) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t keep = (2 * j < vc ? 0x0000FFFFu : 0u) | (2 * j + 1 < vc ? 0xFFFF0000u : 0u);
+      o[j] &= keep;
+    }
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
 
 // Grouped raster over output tiles so that concurrently resident CTAs share A
 // and B panels in L2. group > 0: `group` tile-rows advance together along N;
@@ -213,18 +316,28 @@ __device__ __forceinline__ void epilogue_chunk_lsu(const TcParams& p, float* til
   for (int j = 0; j < 32; ++j) tile[lane * LD + j] = __uint_as_float(r[j]);
   __syncwarp();
   const bool read_c = p.beta != 0.0f;
+  // Every C element of the chunk is loaded before the first store: a load
+  // placed after a store through another pointer cannot be moved ahead of it
+  // (they might alias), so interleaving would make one dependent global round
+  // trip per row.
   if (chunk_is_vector(p, col0)) {
     // lane -> row (lane / 4) of an 8-row band, 8-column group (lane % 4)
     const int cg = (lane & 3) * 8;
+    uint4 prev[4];
+#pragma unroll
+    for (int band = 0; band < 4; ++band) {
+      const int row = row_base + band * 8 + (lane >> 2);
+      prev[band] = make_uint4(0, 0, 0, 0);
+      if (read_c && row < p.M)
+        prev[band] = *reinterpret_cast<const uint4*>(p.C + static_cast<size_t>(row) * p.ldc + col0 + cg);
+    }
 #pragma unroll
     for (int band = 0; band < 4; ++band) {
       const int rr = band * 8 + (lane >> 2);
       const int row = row_base + rr;
       if (row < p.M) {
         half* dst = p.C + static_cast<size_t>(row) * p.ldc + col0 + cg;
-        uint4 prev = make_uint4(0, 0, 0, 0);
-        if (read_c) prev = *reinterpret_cast<const uint4*>(dst);
-        const uint32_t pw[4] = {prev.x, prev.y, prev.z, prev.w};
+        const uint32_t pw[4] = {prev[band].x, prev[band].y, prev[band].z, prev[band].w};
         uint32_t out[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -240,13 +353,22 @@ __device__ __forceinline__ void epilogue_chunk_lsu(const TcParams& p, float* til
     // lane -> column; each store instruction one contiguous 64-byte run
     const int col = col0 + lane;
     if (col < p.N) {
-#pragma unroll 4
-      for (int rr = 0; rr < 32; ++rr) {
-        const int row = row_base + rr;
-        if (row < p.M) {
-          half* dst = p.C + static_cast<size_t>(row) * p.ldc + col;
-          const float prev = read_c ? __half2float(*dst) : 0.0f;
-          *dst = __float2half_rn(fmaf(p.alpha, tile[rr * LD + lane], p.beta * prev));
+      // rows in groups of 8: eight loads in flight per round trip, few registers
+#pragma unroll 1
+      for (int r0 = 0; r0 < 32; r0 += 8) {
+        float prev[8];
+#pragma unroll
+        for (int rr = 0; rr < 8; ++rr) {
+          const int row = row_base + r0 + rr;
+          prev[rr] = (read_c && row < p.M) ? __half2float(p.C[static_cast<size_t>(row) * p.ldc + col])
+                                           : 0.0f;
+        }
+#pragma unroll
+        for (int rr = 0; rr < 8; ++rr) {
+          const int row = row_base + r0 + rr;
+          if (row < p.M)
+            p.C[static_cast<size_t>(row) * p.ldc + col] =
+                __float2half_rn(fmaf(p.alpha, tile[(r0 + rr) * LD + lane], p.beta * prev[rr]));
         }
       }
     }
@@ -329,12 +451,12 @@ __device__ __forceinline__ void splitk_reduce(const TcParams& p, uint32_t part, 
   }
 }
 
-template <int BN, bool PAIR, bool BKM, int SLABS, bool SLAB_N>
-__global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads, 1)
+template <int BN, bool PAIR, bool BKM, int SLABS, bool SLAB_N, bool LSU = false>
+__global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N, LSU>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_c, const TcParams p) {
-  using Cfg = TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>;
+  using Cfg = TcCfg<BN, PAIR, BKM, SLABS, SLAB_N, LSU>;
   constexpr int kStages = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
 
@@ -382,7 +504,8 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
   griddep_launch_dependents();
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(full_bar(s), 1);
+      // LSU: every loader warp arrives once its share of the stage is written
+      mbar_init(full_bar(s), LSU ? Cfg::kEpiWarps : 1);
       mbar_init(empty_bar(s), 1);
     }
     for (int a = 0; a < 2; ++a)
@@ -397,8 +520,10 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
     }
     *abort_flag = 0;
     fence_barrier_init();
-    tma_prefetch_desc(&tmap_a);
-    tma_prefetch_desc(&tmap_b);
+    if (!LSU) {
+      tma_prefetch_desc(&tmap_a);
+      tma_prefetch_desc(&tmap_b);
+    }
     if (p.c_tma) tma_prefetch_desc(&tmap_c);
   }
   if (warp == 1) {
@@ -436,7 +561,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
     // and, for that tile, two idle warps; they hand registers to the epilogue.
     if constexpr (SLAB_N) setmaxnreg_dec<Cfg::kRegsCtl>();
     if (warp == 0) {
-      if (lane == 0) {
+      if (!LSU && lane == 0) {
         // ---------------- TMA producer (every CTA) ----------------
         int stage = 0;
         uint32_t phase = 0;
@@ -750,9 +875,90 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N>::kThreads,
       uint32_t acc_phase = 0;
       bool ok = true;
       constexpr int kChunks = Cfg::kEpiChunks;
+      // LSU: these warps first load the tile's K blocks into the stage ring
+      // (their own ring position, as the TMA producer would keep it).
+      int ld_stage = 0;
+      uint32_t ld_phase = 0;
       for (int t = unit; t < num_tiles && ok; t += num_units) {
         int tm, tn;
         tile_coords(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
+        if constexpr (LSU) {
+          // Chunk u of this thread is segment (tid + kLsuThreads * u) / 8, lane c
+          // of its 8; its address, line phase, valid columns and place in the
+          // stage are recomputed from (u, kb) when needed (registers hold only
+          // the loaded lines). A segment's line phase is the same in every K
+          // block: a K block advances it by 64 halves = 8 lines (A, Bt) or by
+          // 64 rows of B.
+          constexpr int kPer = Cfg::kLsuPer;
+          const int tid = threadIdx.x - 32 * Cfg::kEpiWarp0;  // 0 .. kLsuThreads-1
+          const int c = lane & 7;
+          const int m0 = tm * Cfg::kTileM;
+          const int n0 = tn * Cfg::kTileN;
+          auto geom = [&](int u, int kb, LsuSeg& g) {
+            const int r = (tid + Cfg::kLsuThreads * u) >> 3;
+            const int kx = kb * Cfg::BK;
+            if (r < 128) {
+              g = lsu_seg(p.A, p.lda, p.M, p.K, m0 + r, kx);
+            } else if constexpr (BKM) {
+              g = lsu_seg(p.B, p.ldb, p.N, p.K, n0 + r - 128, kx);
+            } else {
+              const int rb = r - 128;
+              g = lsu_seg(p.B, p.ldb, p.K, p.N, kx + (rb & 63), n0 + 64 * (rb >> 6));
+            }
+          };
+          // the chunk's 16 bytes in the stage (128B swizzle: 16-byte unit c of a
+          // 128-byte row lands at c ^ (row % 8))
+          auto doff = [&](int u, uint32_t sa, uint32_t sb) {
+            const int r = (tid + Cfg::kLsuThreads * u) >> 3;
+            if (r < 128) return sa + static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
+            const int rb = r - 128;
+            if constexpr (BKM) return sb + static_cast<uint32_t>(rb * 128 + ((c ^ (rb & 7)) << 4));
+            const int kk = rb & 63;
+            return sb + static_cast<uint32_t>((rb >> 6) * Cfg::kBBoxBytes + kk * 128 +
+                                              ((c ^ (kk & 7)) << 4));
+          };
+          uint4 v[kPer], x[kPer];
+          if (kb_lo < kb_hi) {
+#pragma unroll
+            for (int u = 0; u < kPer; ++u) {
+              LsuSeg g;
+              geom(u, kb_lo, g);
+              lsu_issue(g, c, v[u], x[u]);
+            }
+          }
+          for (int kb = kb_lo; kb < kb_hi; ++kb) {
+            // registers may be loaded early; the stage must be free before it is written
+            if (!mbar_wait_warp(empty_bar(ld_stage), ld_phase ^ 1u, p.timeout_ns, abort_flag, p.err,
+                                kErrTimeoutProducer)) {
+              ok = false;
+              break;
+            }
+            const uint32_t sa = sA0 + ld_stage * Cfg::kABytes;
+            const uint32_t sb = sB0 + ld_stage * Cfg::kBBytes;
+            const bool more = kb + 1 < kb_hi;
+#pragma unroll
+            for (int u = 0; u < kPer; ++u) {
+              LsuSeg g;
+              geom(u, kb, g);
+              st_shared_v4(doff(u, sa, sb), lsu_assemble(g, c, v[u], x[u]));
+              // this chunk's loads for the next K block go out while the rest
+              // of this one is assembled
+              if (more) {
+                geom(u, kb + 1, g);
+                lsu_issue(g, c, v[u], x[u]);
+              }
+            }
+            // generic-proxy writes -> visible to the tensor core (async proxy)
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full_bar(ld_stage));
+            if (++ld_stage == kStages) {
+              ld_stage = 0;
+              ld_phase ^= 1u;
+            }
+          }
+          if (!ok) break;
+        }
         for (int sl = 0; sl < SLABS && ok; ++sl) {
           const int row_base = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kCtaRows +
                                sl * Cfg::BM + quad * 32;

@@ -169,11 +169,21 @@ def gemm_host(a, b, c, alpha: float = 1.0, beta: float = 0.0, out=None, slabs: i
     Asynchronous like the device entry points: `stream` (a torch.cuda.Stream;
     default: the current stream) is ordered after the last copy back;
     synchronize it before reading `out`.
+
+    B may instead be a contiguous CUDA tensor on the current device (a weight
+    that stays resident, or a replica of B that a multi-GPU job broadcast once):
+    then only A (and C) cross PCIe.
     """
     import torch
+    b_resident = b.is_cuda
     for name, t in (("A", a), ("B", b), ("C", c)) + ((("out", out),) if out is not None else ()):
-        if t.dtype != torch.float16 or t.is_cuda or t.dim() != 2 or not t.is_contiguous():
-            raise GemmError(f"{name} must be a contiguous 2-D float16 host tensor")
+        on_device_ok = name == "B" and b_resident
+        if (t.dtype != torch.float16 or (t.is_cuda and not on_device_ok) or t.dim() != 2
+                or not t.is_contiguous()):
+            raise GemmError(f"{name} must be a contiguous 2-D float16 host tensor"
+                            + (" (B may be a CUDA tensor)" if name == "B" else ""))
+    if b_resident and b.device.index != torch.cuda.current_device():
+        raise GemmError("a device-resident B must be on the current CUDA device")
     m, k = a.shape
     k2, n = b.shape
     if k2 != k or tuple(c.shape) != (m, n) or (out is not None and tuple(out.shape) != (m, n)):
@@ -195,7 +205,7 @@ def gemm_host(a, b, c, alpha: float = 1.0, beta: float = 0.0, out=None, slabs: i
         rows = max(128, (-(-m // slabs)) // 128 * 128)
     bounds = [(r, min(m, r + rows)) for r in range(0, m, rows)]
     a_d = torch.empty((m, k), dtype=torch.float16, device=dev)
-    b_d = torch.empty((k, n), dtype=torch.float16, device=dev)
+    b_d = b if b_resident else torch.empty((k, n), dtype=torch.float16, device=dev)
     c_d = torch.empty((m, n), dtype=torch.float16, device=dev)
     for t in (a_d, b_d, c_d):  # used on the side streams: keep them alive until those finish
         for s in (h2d, comp, d2h):
@@ -203,7 +213,8 @@ def gemm_host(a, b, c, alpha: float = 1.0, beta: float = 0.0, out=None, slabs: i
     h2d.wait_stream(caller)
     b_done = torch.cuda.Event()
     with torch.cuda.stream(h2d):
-        b_d.copy_(b, non_blocking=True)
+        if not b_resident:
+            b_d.copy_(b, non_blocking=True)
         b_done.record(h2d)
     done = None
     for r0, r1 in bounds:

@@ -18,9 +18,19 @@ plain path. Splitting along K would instead round C to FP16 between blocks.
 One process per GPU; the group comes from `torch.distributed`. The compute steps
 are injectable so the host logic (partition, broadcast, gather) is testable on
 CPU ranks with the gloo backend.
+
+Failure detection: the broadcasts take an optional host deadline. The host then
+polls the collective's completion and the communicator's asynchronous error
+state; when the deadline passes or an error appears, it aborts the group's
+communicators (ncclCommAbort under NCCL, which also ends a collective still
+waiting for a peer) and raises CommDeadlineExceeded, so that a rank that died
+or stalled surfaces as an error within the deadline instead of a hang. The
+group that carries broadcast_and_run's blocks uses non-blocking NCCL
+communicators, whose calls never hold the host.
 """
 from __future__ import annotations
 
+import time
 from typing import Callable, Optional
 
 import torch
@@ -29,6 +39,25 @@ import torch.distributed as dist
 from . import gemm as _gpu_gemm
 from . import gemm_sub as _gpu_gemm_sub
 from . import slab_rows
+
+
+class CommDeadlineExceeded(RuntimeError):
+    """A collective did not complete within its host deadline (or its
+    communicator reported an asynchronous error); the group was aborted."""
+
+
+def _gpu_compute_sub(a, b_block, c_view, alpha, beta, max_sms):
+    """The dense kernel on strided views with an SM cap (gemm_launcher_sub).
+    An A slab that the kernel cannot read in place (K % 8 != 0 or a base that
+    is not 16-byte aligned) goes through the regular entry point on contiguous
+    copies instead, without the SM cap."""
+    k = a.shape[1]
+    if k % 8 == 0 and a.data_ptr() % 16 == 0:
+        _gpu_gemm_sub(a, b_block, c_view, alpha, beta, max_sms=max_sms)
+        return
+    c_tmp = c_view.contiguous()
+    _gpu_gemm(a.contiguous(), b_block.contiguous(), c_tmp, alpha, beta)
+    c_view.copy_(c_tmp)
 
 
 class SlabGemm:
@@ -43,56 +72,128 @@ class SlabGemm:
         # compute(a_slab, b, c_slab, alpha, beta) -> None (in place on c_slab)
         self.compute = compute or (lambda a, b, c, alpha, beta: _gpu_gemm(a, b, c, alpha, beta))
         # compute_sub(a_slab, b_block, c_view, alpha, beta, max_sms) -> None, where
-        # c_view is a column block of C (row pitch = C's width)
-        self.compute_sub = compute_sub or (
-            lambda a, b, c, alpha, beta, max_sms: _gpu_gemm_sub(a, b, c, alpha, beta,
-                                                                max_sms=max_sms))
+        # b_block may be a row-strided view and c_view is a column block of C
+        # (row pitch = C's width)
+        self.compute_sub = compute_sub or _gpu_compute_sub
 
     def partition(self, m: int) -> tuple[int, int]:
         """(row0, rows) of this rank's C slab."""
         return slab_rows(m, self.world, self.rank)
 
-    def broadcast_b(self, b: torch.Tensor, src: int = 0) -> torch.Tensor:
-        """Replicate B from `src` into `b` on every rank (in place), once."""
-        dist.broadcast(b, src=src, group=self.group)
+    def broadcast_b(self, b: torch.Tensor, src: int = 0,
+                    deadline_s: Optional[float] = None) -> torch.Tensor:
+        """Replicate B from `src` into `b` on every rank (in place), once.
+        With `deadline_s`, the host waits at most that long for the broadcast
+        to complete (see await_works)."""
+        if deadline_s is None:
+            dist.broadcast(b, src=src, group=self.group)
+            return b
+        work = dist.broadcast(b, src=src, group=self.group, async_op=True)
+        self.await_works([work], deadline_s, self.group, "broadcast of B")
         return b
 
     @staticmethod
-    def broadcast_group(ranks: list[int], max_ctas: int) -> dist.ProcessGroup:
+    def _comm_error(group) -> Optional[str]:
+        """The asynchronous error state of the group's NCCL communicators
+        (ncclCommGetAsyncError as torch reports it), or None."""
+        pg = group if group is not None else dist.distributed_c10d._get_default_group()
+        try:
+            backend = pg._get_backend(torch.device("cuda"))
+        except Exception:
+            return None
+        get_error = getattr(backend, "get_error", None)
+        if get_error is None:
+            return None
+        err = str(get_error())
+        return None if err.endswith("SUCCESS") else err
+
+    @staticmethod
+    def abort(group) -> None:
+        """Abort the group's communicators (ncclCommAbort for NCCL). Backends
+        without an abort (gloo) are left to their own process-group timeout."""
+        pg = group if group is not None else dist.distributed_c10d._get_default_group()
+        try:
+            pg.abort()
+        except Exception:
+            pass
+
+    def await_works(self, works, deadline_s: float, group, what: str) -> None:
+        """Poll `works` (async collective handles) on the host until all have
+        completed, for at most `deadline_s` seconds. If the deadline passes, or
+        the communicator reports an asynchronous error first, abort the group
+        and raise CommDeadlineExceeded; an error the backend raised itself is
+        re-raised as CommDeadlineExceeded too, after the same abort."""
+        t0 = time.monotonic()
+        try:
+            while True:
+                if all(w.is_completed() for w in works):
+                    for w in works:
+                        w.wait()
+                    return
+                err = self._comm_error(group)
+                if err is not None:
+                    raise CommDeadlineExceeded(f"{what}: communicator error {err}")
+                if time.monotonic() - t0 > deadline_s:
+                    raise CommDeadlineExceeded(
+                        f"{what}: not complete after {deadline_s:.3g} s (a peer stalled or died)")
+                time.sleep(0.0005)
+        except CommDeadlineExceeded:
+            self.abort(group)
+            raise
+        except Exception as e:
+            self.abort(group)
+            raise CommDeadlineExceeded(f"{what}: {type(e).__name__}: {e}") from e
+
+    @staticmethod
+    def broadcast_group(ranks: list[int], max_ctas: int,
+                        nonblocking: bool = True) -> dist.ProcessGroup:
         """A NCCL group for broadcast_and_run whose collectives use at most
         `max_ctas` CTAs, on a high-priority stream. With the GEMM leaving that
         many SMs free, every broadcast CTA finds an SM. Otherwise a ring
         channel whose CTA cannot be scheduled stalls its peers until the GEMM
-        ends, and the overlap is lost. Collective: every rank calls it."""
+        ends, and the overlap is lost. Its communicators are non-blocking
+        (NCCL config `blocking = 0`), so a deadline can abort them. Collective:
+        every rank calls it."""
         opts = dist.ProcessGroupNCCL.Options()
         opts.config.max_ctas = max_ctas
         opts.config.min_ctas = 1
+        if nonblocking:
+            opts.config.blocking = 0
         opts.is_high_priority_stream = True
         return dist.new_group(ranks=ranks, backend="nccl", pg_options=opts)
 
     def broadcast_and_run(self, a_slab: torch.Tensor, b: torch.Tensor, c_slab: torch.Tensor,
                           alpha: float = 1.0, beta: float = 0.0, src: int = 0, chunks: int = 8,
-                          reserve_sms: int = 16) -> list[torch.Tensor]:
+                          reserve_sms: int = 16,
+                          deadline_s: Optional[float] = None) -> list[torch.Tensor]:
         """broadcast_b(b, src) followed by run(...), overlapped.
 
         B[K, N] (filled on `src`; its contents elsewhere are ignored) is split
-        into `chunks` column blocks. On `src` each block is packed contiguously,
+        into `chunks` column blocks (widths rounded up to multiples of 8; the
+        last block takes the rest). On `src` each block is packed,
         and all blocks are broadcast asynchronously in order. Each rank's stream
         waits for block j, then computes C[:, block j] = alpha * A @ B[:, block j]
         + beta * C[:, block j] while blocks j+1.. are in flight. Until the last
         block, the GEMM leaves `reserve_sms` SMs free, because the collective's
         kernels cannot start while a persistent GEMM holds every SM. Returns the
         blocks, which hold this rank's replica of B in column-block layout.
-        Ranks must call it collectively with the same chunks."""
+        Ranks must call it collectively with the same chunks. With
+        `deadline_s`, the host then waits at most that long for every block
+        to arrive (await_works), so the call returns only after the broadcast."""
         k, n = b.shape
-        width = -(-n // chunks)
+        # block widths are multiples of 8 columns (the last one takes the rest),
+        # and every block is stored with a row pitch rounded up to 8 halves, so
+        # each is a TMA-addressable operand of the dense kernel whatever N is
+        width = -(-(-(-n // chunks)) // 8) * 8
         bounds = [(c0, min(n, c0 + width)) for c0 in range(0, n, width)]
         blocks, works = [], []
         for c0, c1 in bounds:
-            blk = torch.empty((k, c1 - c0), dtype=b.dtype, device=b.device)
+            pitch = -(-(c1 - c0) // 8) * 8
+            store = torch.empty((k, pitch), dtype=b.dtype, device=b.device)
+            blk = store[:, :c1 - c0]
             if self.rank == src:
                 blk.copy_(b[:, c0:c1])
-            works.append(dist.broadcast(blk, src=src, group=self.bcast_group, async_op=True))
+            works.append(dist.broadcast(store, src=src, group=self.bcast_group, async_op=True))
             blocks.append(blk)
         total_sms = (torch.cuda.get_device_properties(b.device).multi_processor_count
                      if b.is_cuda else 0)
@@ -102,6 +203,8 @@ class SlabGemm:
             max_sms = max(2, total_sms - reserve_sms) if (pending and total_sms) else 0
             if a_slab.shape[0]:
                 self.compute_sub(a_slab, blk, c_slab[:, c0:c1], alpha, beta, max_sms)
+        if deadline_s is not None:
+            self.await_works(works, deadline_s, self.bcast_group, "column-block broadcast of B")
         return blocks
 
     def run(self, a_slab: torch.Tensor, b: torch.Tensor, c_slab: torch.Tensor, alpha: float = 1.0,

@@ -23,6 +23,7 @@ os.environ.setdefault("GEMM_LAUNCH_LOG", "0")
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 GPU (sm_100a)")
+    config.addinivalue_line("markers", "multigpu: needs two or more B200 GPUs (run on its own)")
 
 
 @pytest.fixture(scope="session")

@@ -16,7 +16,7 @@ from oracle import oracle
 
 pytestmark = pytest.mark.gpu
 
-PATH_TC, PATH_ROWS, PATH_COL, PATH_ROWS_LSU, PATH_COL_LSU, PATH_DEC = 1, 2, 3, 4, 5, 6
+PATH_TC, PATH_ROWS, PATH_COL, PATH_ROWS_LSU, PATH_COL_LSU, PATH_DEC, PATH_TC_LSU = 1, 2, 3, 4, 5, 6, 7
 
 
 def _go(lib, cuda, m, n, k, alpha=1.0, beta=0.0, **kw):
@@ -58,6 +58,67 @@ TC_SHAPES = [(128, 256, 64), (256, 512, 128), (129, 257, 65), (1, 8, 8), (127, 2
 def test_tc_path(lib, cuda, shape, tile_n):
     m, n, k = shape
     _go(lib, cuda, m, n, k, 0.75, 0.5, dist="normal", path=PATH_TC, tile_n=tile_n, seed=m + n + k)
+
+
+# The tile kernel with per-thread operand loads (path 7: A and B read in place at
+# any alignment and pitch, no repack): every single-CTA tile, ragged M/N/K, each
+# pointer at half offsets 0, 1 and 3 (phases of the 16-byte lines), K and N that
+# are not multiples of 8 (rows of alternating phase), beta = 0 over NaN C.
+LSU_SHAPES = [(128, 256, 64), (129, 257, 65), (1023, 2049, 777), (300, 1000, 72), (17, 19, 23),
+              (513, 264, 200), (640, 384, 4104), (1000, 2056, 136), (256, 130, 1031)]
+
+
+@pytest.mark.parametrize("tile_n", [64, 128, 256], ids=["128x64", "128x128", "128x256"])
+@pytest.mark.parametrize("shape", LSU_SHAPES, ids=str)
+@pytest.mark.parametrize("offsets", [(0, 0, 0), (1, 1, 1), (3, 1, 0), (0, 3, 1)], ids=str)
+def test_tc_lsu_path(lib, cuda, shape, tile_n, offsets):
+    m, n, k = shape
+    beta = 0.0 if offsets[0] == 3 else -0.25
+    _go(lib, cuda, m, n, k, 0.75, beta, dist="normal", path=PATH_TC_LSU, tile_n=tile_n,
+        offsets=offsets, seed=m + n + k + sum(offsets))
+
+
+@pytest.mark.parametrize("tile,ks", [(64, 4), (128, 2), (128, 8), (256, 4)], ids=str)
+def test_tc_lsu_split_k(lib, cuda, monkeypatch, tile, ks):
+    monkeypatch.setenv("GEMM_SPLITK_TILE", str(tile))
+    monkeypatch.setenv("GEMM_SPLITK_KS", str(ks))
+    _go(lib, cuda, 300, 1001, 4097, 0.75, -0.5, dist="normal", path=PATH_TC_LSU,
+        offsets=(1, 1, 1), seed=tile + ks)
+
+
+@pytest.mark.parametrize("lsu", ["1", "-1"], ids=["lsu", "repack"])
+@pytest.mark.parametrize("shape", [(1023, 2049, 777), (129, 257, 65), (2048, 1024, 1001)], ids=str)
+def test_misaligned_dense_both_feeds(lib, cuda, monkeypatch, lsu, shape):
+    """The automatic dispatch on misaligned operands through either operand feed:
+    in-place per-thread loads or the repack into scratch."""
+    import gemm_b200
+    monkeypatch.setenv("GEMM_LSU", lsu)
+    m, n, k = shape
+    _go(lib, cuda, m, n, k, 0.75, -0.25, offsets=(1, 1, 1), seed=m + k, fn="launcher")
+    assert ("lsu" in gemm_b200.last_kernel()) == (lsu == "1"), gemm_b200.last_kernel()
+
+
+def test_misaligned_dense_allocates_nothing(lib, cuda):
+    """The reference's misaligned dense config through gemm_launcher: one kernel,
+    operands read in place, so no call takes device memory (free memory is
+    unchanged across 100 calls that start from a fresh shape)."""
+    import gemm_b200
+    m, n, k = 1023, 2049, 777
+    ga = Guarded((m, k), cuda, fill=0.5, offset=65)
+    gb = Guarded((k, n), cuda, fill=0.25, offset=65)
+    gc = Guarded((m, n), cuda, fill=1.0, offset=65)
+    f = ctypes.c_float
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(100):
+        lib.gemm_launcher(ga.tensor.data_ptr(), gb.tensor.data_ptr(), gc.tensor.data_ptr(), m, n, k,
+                          f(0.75), f(-0.25))
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert lib.gemm_launcher_status() == 0
+    assert "lsu" in gemm_b200.last_kernel()
+    assert free1 == free0, f"free device memory moved by {free0 - free1} bytes"
+    assert gc.canaries_ok()
 
 
 # Cluster split-K on 128 x 256 tiles (tile code 5): ragged M, N and K, the

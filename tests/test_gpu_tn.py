@@ -2,7 +2,8 @@
 
 Same tcgen05 kernels with B read K-major; checked against the CPU oracle on
 every tile shape, across tile and K-block edges, with misaligned pointers
-(repack path) and with beta = 0 on a NaN-filled C.
+(read in place by per-thread loads, or repacked) and with beta = 0 on a
+NaN-filled C.
 """
 import ctypes
 
@@ -18,8 +19,10 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.parametrize("tile", [0, 64, 128, 256, 2, 3, 4])
 @pytest.mark.parametrize("shape", [(128, 256, 64), (129, 257, 65), (300, 1000, 72), (1, 8, 8),
                                    (1024, 1024, 1024), (640, 384, 4104), (17, 19, 23)], ids=str)
-@pytest.mark.parametrize("offset,beta", [(0, 0.0), (1, 0.5)])
-def test_tn_matches_oracle(lib, cuda, shape, tile, offset, beta):
+@pytest.mark.parametrize("offset,beta,feed", [(0, 0.0, "0"), (1, 0.5, "1"), (1, 0.5, "-1")],
+                         ids=["aligned", "misaligned-lsu", "misaligned-repack"])
+def test_tn_matches_oracle(lib, cuda, monkeypatch, shape, tile, offset, beta, feed):
+    monkeypatch.setenv("GEMM_LSU", feed)  # misaligned Bt/A: read in place, or repacked
     m, n, k = shape
     a, b, c0 = oracle.make_inputs(m, n, k, "normal", seed=m + 3 * n + k)
     bt = b.t().contiguous()

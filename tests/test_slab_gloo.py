@@ -2,9 +2,11 @@
 
 The compute step is the CPU oracle (tests may use it as the checker), so these
 cover partition, broadcast of B, per-rank slab work and reassembly without a
-GPU. The failure test makes one rank die before the broadcast and checks that
-the surviving rank gets an error from its collective within the process-group
-timeout instead of hanging (host-side failure injection; no GPU is involved).
+GPU. The failure tests inject on the host, with no GPU involved: one rank dies
+before the broadcast, and the surviving rank must get an error from its
+collective within the process-group timeout instead of hanging; or one rank
+stays alive but never joins, and the other's host deadline (shorter than the
+process-group timeout) must end its broadcast with CommDeadlineExceeded.
 """
 import multiprocessing as mp
 import os
@@ -39,7 +41,7 @@ def _rank_main(rank, world, port, scenario, q):
                                 timeout=timedelta(seconds=5))
         m, n, k, alpha, beta = 37, 24, 40, 0.75, -0.25
         if scenario == "overlapped":
-            n = 26  # three column blocks of 9, 9 and 8
+            n = 37  # column blocks of 16, 16 and 5 (widths rounded up to multiples of 8)
         a, b_full, c = oracle.make_inputs(m, n, k, "uniform", seed=11)
 
         def cpu_compute(a_s, b_s, c_s, al, be):
@@ -55,7 +57,7 @@ def _rank_main(rank, world, port, scenario, q):
             a_slab = a[row0:row0 + rows].contiguous()
             c_slab = c[row0:row0 + rows].clone()
             blocks = sg.broadcast_and_run(a_slab, b, c_slab, alpha, beta, chunks=3)
-            assert [t.shape[1] for t in blocks] == [9, 9, 8]
+            assert [t.shape[1] for t in blocks] == [16, 16, 5]
             assert torch.equal(torch.cat(blocks, dim=1), b_full)
             plain = c[row0:row0 + rows].clone()
             cpu_compute(a_slab, b_full, plain, alpha, beta)
@@ -71,10 +73,18 @@ def _rank_main(rank, world, port, scenario, q):
             return
         if scenario == "die_before_broadcast" and rank == 1:
             os._exit(3)  # this rank disappears without joining the collective
+        if scenario == "stall_before_broadcast" and rank == 1:
+            time.sleep(12)  # alive, but never joins the collective
+            q.put((rank, "stalled", None, None))
+            os._exit(0)
         b = b_full.clone() if rank == 0 else torch.zeros_like(b_full)
         t0 = time.time()
         try:
-            sg.broadcast_b(b)
+            if scenario == "stall_before_broadcast":
+                # host deadline well below the 5 s process-group timeout
+                sg.broadcast_b(b, deadline_s=1.0)
+            else:
+                sg.broadcast_b(b)
         except Exception as e:  # the surviving rank must see an error, not hang
             q.put((rank, "collective_error", round(time.time() - t0, 2), type(e).__name__))
             return
@@ -137,3 +147,14 @@ def test_dead_rank_surfaces_as_error_not_hang():
     assert len(results) == 1 and results[0][0] == 0, results
     assert results[0][1] == "collective_error", results
     assert results[0][2] < 30
+
+
+def test_stalled_rank_hits_host_deadline():
+    """A peer that is alive but never joins: the broadcast's host deadline (1 s)
+    ends the wait well before the 5 s process-group timeout."""
+    results, alive = _spawn(2, "stall_before_broadcast", wait_s=60)
+    assert not alive, "a rank hung"
+    by_rank = {r[0]: r for r in results}
+    assert by_rank[0][1] == "collective_error", results
+    assert by_rank[0][3] == "CommDeadlineExceeded", results
+    assert by_rank[0][2] < 4.0, results

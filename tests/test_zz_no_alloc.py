@@ -3,17 +3,29 @@
 Some callers cannot let a library allocate device memory: serving processes
 that reserve nearly all HBM for their own pools up front, and frameworks whose
 allocator must account for every device byte. gemm_launcher_noalloc serves
-them: where the tensor-core path has to repack a misaligned or odd-pitched A
-or B, it uses a fixed 32 MiB device buffer compiled into the library instead
-of cudaMallocAsync. These tests call it through the C ABI on the shapes that
-need that repack (and on ones that do not), twice in a row on the same
-inputs, and compare each result with the allocating entry point's result
-under the same tolerance rules as every other parity test. A shape whose
-repack exceeds 32 MiB must be refused before anything is launched.
+them: where gemm_launcher_stream's plan for a call would take repack scratch
+(a misaligned or odd-pitched A or B on a problem large enough for the
+tensor-core path to repack it), it uses a fixed 32 MiB device buffer compiled
+into the library instead of cudaMallocAsync; every other call runs exactly as
+gemm_launcher_stream, whose other kernels allocate nothing.
+
+The comparison tests call it through the C ABI twice in a row on the same
+inputs, with the repack feed forced (GEMM_LSU=-1, so that the fixed buffer is
+used on every misaligned shape) and with the default feed, and compare each
+result with the allocating entry point's under the same tolerance rules as
+every other parity test. A separate test runs in a fresh process, checks from
+the launch log that the repack kernels wrote into the fixed buffer, and checks
+that free device memory does not move across calls on shapes that process has
+never run. A shape whose repack exceeds 32 MiB must be refused before anything
+is launched.
 
 The file is named so that pytest collects it last.
 """
 import ctypes
+import os
+import subprocess
+import sys
+from pathlib import Path
 
 import pytest
 import torch
@@ -22,6 +34,8 @@ from gpu_harness import Guarded
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
+
+REPO = Path(__file__).resolve().parent.parent
 
 CASES = [
     # (M, N, K, alpha, beta, offset of A/B/C in halves)
@@ -56,8 +70,10 @@ def _run(lib, fn, ga, gb, c0, m, n, k, alpha, beta, off, cuda):
     return rc, gc.tensor.cpu()
 
 
+@pytest.mark.parametrize("feed", ["-1", "0"], ids=["repack-feed", "default-feed"])
 @pytest.mark.parametrize("case", CASES, ids=str)
-def test_noalloc_matches_allocating_entry_point(lib, cuda, case):
+def test_noalloc_matches_allocating_entry_point(lib, cuda, monkeypatch, case, feed):
+    monkeypatch.setenv("GEMM_LSU", feed)
     m, n, k, alpha, beta, off = case
     a, b, c0, ga, gb = _setup(cuda, m, n, k, beta, off, seed=m + n + k)
     rc_ref, expected = _run(lib, lambda *x: lib.gemm_launcher_stream(*x) or 0, ga, gb, c0, m, n, k,
@@ -69,11 +85,65 @@ def test_noalloc_matches_allocating_entry_point(lib, cuda, case):
         assert rc == 0
         chk = oracle.check(got, expected.float())
         assert chk.passed, f"noalloc vs allocating entry point {case}: {chk}"
+        # the same plan (tile, K split) as the allocating entry point: identical bits
+        assert torch.equal(got, expected), f"noalloc differs in bits from the allocating path {case}"
         assert oracle.check(got, ref32).passed
     assert torch.equal(ga.tensor.cpu(), a) and torch.equal(gb.tensor.cpu(), b)
 
 
-def test_noalloc_refuses_repack_beyond_its_buffer(lib, cuda, capfd):
+_FRESH_PROCESS = r"""
+import ctypes, sys
+sys.path[:0] = [sys.argv[1], sys.argv[1] + "/gemm-project_b200"]
+import torch
+import gemm_b200
+lib = gemm_b200.load()
+dev = torch.device("cuda:0")
+f = ctypes.c_float
+
+def make(m, n, k):
+    # one half past each allocation's base: not 16-byte aligned
+    return [torch.full((r * c + 1,), 0.5, dtype=torch.float16, device=dev)[1:]
+            for r, c in ((m, k), (k, n), (m, n))]
+
+def call(m, n, k, bufs):
+    a, b, c = bufs
+    rc = lib.gemm_launcher_noalloc(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k,
+                                   f(1.0), f(0.0), None)
+    torch.cuda.synchronize()
+    assert rc == 0 and lib.gemm_launcher_status() == 0, rc
+
+shapes = [(300, 520, 1001), (2000, 2056, 3001), (1500, 3000, 2049)]
+bufs = [make(*s) for s in shapes]         # every input allocated before the measurement
+torch.cuda.synchronize()
+call(*shapes[0], bufs[0])                 # first call: library set-up on this device
+free0 = torch.cuda.mem_get_info()[0]
+for s, bb in zip(shapes[1:], bufs[1:]):   # shapes this process has never run
+    call(*s, bb)
+    call(*s, bb)
+free1 = torch.cuda.mem_get_info()[0]
+print(f"FREE_DELTA {free0 - free1}", flush=True)
+"""
+
+
+def test_noalloc_uses_fixed_buffer_in_fresh_process(lib, cuda):
+    """Repack shapes never seen by the process: the launch log shows the repack
+    kernels writing into the fixed buffer, and free device memory does not move
+    across the calls (modules load eagerly in that process, so a kernel's first
+    launch takes no memory either)."""
+    env = dict(os.environ, GEMM_LSU="-1", GEMM_LAUNCH_LOG="1", CUDA_MODULE_LOADING="EAGER")
+    proc = subprocess.run([sys.executable, "-c", _FRESH_PROCESS, str(REPO)], capture_output=True,
+                          text=True, env=env, timeout=300)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    out = proc.stdout
+    assert "pack_rows_kernel<A,static>: M=2000 N=2056 K=3001" in out, out[-3000:]
+    assert "pack_rows_kernel<B,static>: M=1500 N=3000 K=2049" in out, out[-3000:]
+    assert "pack_rows_kernel<A>:" not in out and "pack_rows_kernel<B>:" not in out
+    delta = [int(ln.split()[1]) for ln in out.splitlines() if ln.startswith("FREE_DELTA")]
+    assert delta == [0], out[-2000:]
+
+
+def test_noalloc_refuses_repack_beyond_its_buffer(lib, cuda, monkeypatch, capfd):
+    monkeypatch.setenv("GEMM_LSU", "-1")
     # odd K: A would be repacked to 4200 x 4104 halves = 34.5 MB > 32 MiB
     m, n, k = 4200, 256, 4097
     ga = Guarded((m, k), cuda, fill=1.0)
