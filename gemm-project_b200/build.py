@@ -29,7 +29,7 @@ EXPORTS = [
     "gemm_launcher", "gemm_launcher_stream", "gemm_launcher_ex", "gemm_launcher_status",
     "gemm_last_kernel", "gemm_cublas", "gemm_cublas_stream", "gemm_slab_rows",
     "gemm_selftest_wait_timeout", "gemm_launcher_noalloc", "gemm_launcher_tn",
-    "launchGemmSample", "gemm_launch_error", "gemm_launcher_sub",
+    "launchGemmSample", "gemm_launch_error", "gemm_launcher_sub", "gemm_selftest_stall",
 ]
 
 

@@ -64,6 +64,10 @@ constexpr int kMaxDevices = 64;
 
 thread_local int tl_status = 0;
 thread_local const char* tl_last_kernel = "";
+// Failure-detection self test (gemm_selftest_stall): while non-zero, tile
+// kernels launched by this thread load no operand and bound every wait by this
+// many nanoseconds.
+thread_local unsigned long long tl_stall_ns = 0;
 
 struct DeviceInfo {
   int sms = 0;
@@ -129,7 +133,7 @@ void configure_tc() {
   cudaFuncSetAttribute(tc_gemm_kernel<BN, PAIR, true, SLABS, SLAB_N>,
                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                        TcCfg<BN, PAIR, true, SLABS, SLAB_N>::kSmemBytes);
-  if constexpr (!PAIR && SLABS == 1 && !SLAB_N) {
+  if constexpr (!PAIR && SLABS == 1 && !SLAB_N && BN <= 128) {
     cudaFuncSetAttribute(tc_gemm_kernel<BN, false, false, 1, false, true>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                          TcCfg<BN, false, false, 1, false, true>::kSmemBytes);
@@ -390,18 +394,19 @@ struct SplitPlan {
   int ks;    // K parts per cluster; 1 = no split
 };
 
-SplitPlan split_k_plan(int M, int N, int K, const DeviceInfo& d) {
-  const SplitPlan none{256, 1};
+SplitPlan split_k_plan(int M, int N, int K, const DeviceInfo& d, int max_tile = 256) {
+  const SplitPlan none{max_tile, 1};
   if (env_int("GEMM_SPLITK") < 0) return none;
   const int num_kb = ceil_div(K, 64);
   const int f_tile = env_int("GEMM_SPLITK_TILE"), f_ks = env_int("GEMM_SPLITK_KS");
-  if ((f_tile == 64 || f_tile == 128 || f_tile == 256) &&
+  if ((f_tile == 64 || f_tile == 128 || f_tile == 256) && f_tile <= max_tile &&
       (f_ks == 1 || f_ks == 2 || f_ks == 4 || f_ks == 8) && num_kb > f_ks * (f_ks - 1))
     return SplitPlan{f_tile, f_ks};
   if (!few_dense_tiles(M, N, d)) return none;  // large: the unsplit tiles
   SplitPlan best = none;
   float best_us = 1e30f;
   for (const int tile : {64, 128, 256}) {
+    if (tile > max_tile) break;
     const int tiles = ceil_div(M, 128) * ceil_div(N, tile);
     const float per_kb = tile == 256 ? 0.36f : (tile == 128 ? 0.26f : 0.24f);
     const float store = tile == 64 ? 1.5f : 2.0f;
@@ -485,13 +490,12 @@ void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
       {"tc_gemm_kernel<128x64,tn>", "tc_gemm_kernel<128x128,tn>", "tc_gemm_kernel<128x256,tn>",
        "tc_gemm_kernel<256x256,pair,tn>", "tc_gemm_kernel<512x256,pair,tn>",
        "tc_gemm_kernel<256x512,pair,tn>"}};
-  static const char* lsu_names[2][3] = {
-      {"tc_gemm_kernel<128x64,lsu>", "tc_gemm_kernel<128x128,lsu>", "tc_gemm_kernel<128x256,lsu>"},
-      {"tc_gemm_kernel<128x64,tn,lsu>", "tc_gemm_kernel<128x128,tn,lsu>",
-       "tc_gemm_kernel<128x256,tn,lsu>"}};
+  static const char* lsu_names[2][2] = {
+      {"tc_gemm_kernel<128x64,lsu>", "tc_gemm_kernel<128x128,lsu>"},
+      {"tc_gemm_kernel<128x64,tn,lsu>", "tc_gemm_kernel<128x128,tn,lsu>"}};
   const int idx =
       PAIR ? (SLAB_N ? 5 : (SLABS == 2 ? 4 : 3)) : (BN == 64 ? 0 : (BN == 128 ? 1 : 2));
-  const char* name = LSU ? lsu_names[BKM ? 1 : 0][idx < 3 ? idx : 0] : names[BKM ? 1 : 0][idx];
+  const char* name = LSU ? lsu_names[BKM ? 1 : 0][idx == 0 ? 0 : 1] : names[BKM ? 1 : 0][idx];
   cudaLaunchConfig_t cfg{};
   cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
@@ -535,13 +539,14 @@ void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
 // that are TMA-addressable as given (pitches lda/ldb in elements).
 // b_kmajor: B is given as Bt[N,K] (row pitch ldb), i.e. C = A * Bt^T.
 // lsu: A and B are read with per-thread loads (any alignment and pitch, no
-// tensor maps); single-CTA tiles (64, 128, 256) only.
+// tensor maps); the 128 x 64 and 128 x 128 tiles only (a 128 x 256 tile's
+// loader would need more registers than its 320 threads can hold).
 int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half* C, int M, int N,
                    int K, float alpha, float beta, cudaStream_t s, int tile, const DeviceInfo& d,
                    bool b_kmajor = false, int ldc = 0, int max_sms = 0, int ksplit = 1,
                    bool lsu = false) {
   if (ldc <= 0) ldc = N;
-  if (lsu && tile != 64 && tile != 128 && tile != 256) tile = 256;
+  if (lsu && tile != 64) tile = 128;
   const bool pair = tile == kTilePair || tile == kTilePair2 || tile == kTilePairN;
   const int slabs = tile == kTilePair2 ? 2 : 1;  // A slabs per CTA
   CUtensorMap ta, tb, tc;
@@ -580,7 +585,8 @@ int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half*
   p.group = raster_group(p.tiles_m, p.tiles_n);
   p.c_tma = c_tma;
   p.c_vec_ok = aligned16(C) && ldc % 8 == 0;
-  p.timeout_ns = wait_timeout_ns();
+  p.timeout_ns = tl_stall_ns ? tl_stall_ns : wait_timeout_ns();
+  p.stall = tl_stall_ns != 0;
   p.err = d.err;
   p.ksplit = 1;
   p.kb_per = p.num_kb;
@@ -594,17 +600,11 @@ int launch_tc_core(const half* a_src, int lda, const half* b_src, int ldb, half*
   p.ldb = ldb;
   if (lsu) {
     if (b_kmajor) {
-      switch (tile) {
-        case 64: launch_tc_bn<64, false, true, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
-        case 128: launch_tc_bn<128, false, true, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
-        default: launch_tc_bn<256, false, true, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
-      }
+      if (tile == 64) launch_tc_bn<64, false, true, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms);
+      else launch_tc_bn<128, false, true, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms);
     } else {
-      switch (tile) {
-        case 64: launch_tc_bn<64, false, false, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
-        case 128: launch_tc_bn<128, false, false, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
-        default: launch_tc_bn<256, false, false, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms); break;
-      }
+      if (tile == 64) launch_tc_bn<64, false, false, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms);
+      else launch_tc_bn<128, false, false, 1, false, true>(ta, tb, tc, p, d, s, M, N, K, max_sms);
     }
     return 0;
   }
@@ -696,13 +696,13 @@ bool use_lsu(int M, int N, int K) {
   return 2.0 * M * N * K <= kLsuMaxFlops;
 }
 
-// Tile choice among the single-CTA tiles (those the LSU variant has).
+// Tile choice among the tiles the LSU variant has (128 x 128, 128 x 64).
 int choose_tile_single(int M, int N, const DeviceInfo& d) {
   const int forced = env_int("GEMM_TILE");
-  if (forced == 64 || forced == 128 || forced == 256) return forced;
-  int best = 256;
+  if (forced == 64 || forced == 128) return forced;
+  int best = 128;
   float best_cost = 1e30f;
-  for (const int bn : {256, 128, 64}) {
+  for (const int bn : {128, 64}) {
     const long tiles = static_cast<long>(ceil_div(M, 128)) * ceil_div(N, bn);
     const long waves = (tiles + d.sms - 1) / d.sms;
     const float eff = bn == 256 ? 0.95f : (bn == 128 ? 0.8f : 0.6f);
@@ -726,24 +726,24 @@ struct TcPlan {
 
 TcPlan plan_tc(const half* A, const half* B, int M, int N, int K, int tile, const DeviceInfo& d,
                bool force_lsu) {
+  const bool aligned = a_tma_ok(A, K) && b_tma_ok(B, N);
+  const bool lsu = force_lsu || (!aligned && use_lsu(M, N, K));
   int ksplit = 1;
   if (tile == 0 || tile == kTileSplitK) {
-    const SplitPlan plan = split_k_plan(M, N, K, d);
+    const SplitPlan plan = split_k_plan(M, N, K, d, lsu ? 128 : 256);
     ksplit = plan.ks;
     if (tile == kTileSplitK) {
       // a forced request: 128 x 256 tiles, split at least in two
       const int num_kb = ceil_div(K, 64);
-      if (plan.tile != 256 || ksplit == 1) ksplit = num_kb > 2 ? 2 : 1;
-      tile = 256;
+      if (ksplit == 1 || (plan.tile != 256 && !lsu)) ksplit = num_kb > 2 ? 2 : 1;
+      tile = lsu ? 128 : 256;
     } else if (ksplit > 1) {
       tile = plan.tile;
     }
   }
   if (tile != 0 && !tile_available(tile, d)) tile = 256;
-  const bool aligned = a_tma_ok(A, K) && b_tma_ok(B, N);
-  const bool lsu = force_lsu || (!aligned && use_lsu(M, N, K));
   if (tile == 0) tile = lsu ? choose_tile_single(M, N, d) : choose_tile(M, N, d);
-  if (lsu && tile != 64 && tile != 128) tile = 256;  // single-CTA tiles only
+  if (lsu && tile != 64) tile = 128;  // the tiles the LSU variant has
   return TcPlan{tile, ksplit, lsu, !lsu && !aligned};
 }
 
@@ -1156,7 +1156,7 @@ int launch_tn(const half* A, const half* Bt, half* C, int M, int N, int K, float
   const bool b_ok = aligned16(Bt) && K % 8 == 0;
   if (!(a_ok && b_ok) && use_lsu(M, N, K)) {
     // read in place by the LSU variant (B K-major): no repack, no scratch
-    if (tile != 64 && tile != 128 && tile != 256) tile = choose_tile_single(M, N, d);
+    if (tile != 64 && tile != 128) tile = choose_tile_single(M, N, d);
     return launch_tc_core(A, K, Bt, K, C, M, N, K, alpha, beta, s, tile, d, /*b_kmajor=*/true,
                           /*ldc=*/0, /*max_sms=*/0, /*ksplit=*/1, /*lsu=*/true);
   }
@@ -1357,6 +1357,18 @@ extern "C" GEMM_API int gemm_launcher_noalloc(const half* A, const half* B, half
   void* scratch = noalloc_scratch_ptr();
   if (scratch == nullptr) return -1;
   return launch_tc_planned(A, B, C, M, N, K, alpha, beta, stream, plan, d, scratch);
+}
+
+extern "C" GEMM_API int gemm_selftest_stall(const half* A, const half* B, half* C, int M, int N,
+                                            int K, int path, int tile_n, int timeout_us,
+                                            cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || (path != 1 && path != 7) || timeout_us <= 0) return -1;
+  tl_stall_ns = static_cast<unsigned long long>(timeout_us) * 1000ull;
+  const int rc = dispatch(A, B, C, M, N, K, 1.0f, 0.0f, stream, path, tile_n);
+  tl_stall_ns = 0;
+  if (rc != 0) return -1;
+  record_error(cudaStreamSynchronize(stream));
+  return gemm_launcher_status();
 }
 
 extern "C" GEMM_API int gemm_selftest_wait_timeout(int timeout_us, cudaStream_t stream) {

@@ -20,7 +20,7 @@ namespace gemm_b200 {
 // ---------------------------------------------------------------------------
 enum DeviceError : int {
   kErrNone = 0,
-  kErrTimeoutProducer = 1,    // TMA producer waited too long for a free stage
+  kErrTimeoutProducer = 1,    // TMA producer or operand loader waited too long for a free stage
   kErrTimeoutMma = 2,         // MMA issuer waited too long for a loaded stage / free accumulator
   kErrTimeoutEpilogue = 3,    // epilogue waited too long for a finished accumulator
   kErrTimeoutCluster = 4,     // cluster barrier in the skinny kernel

@@ -90,10 +90,7 @@ struct TcCfg {
   // cycles per stage with no loads and no UMMAs), so the 128x64, 128x128 and
   // 256x256 pair tiles carry two K blocks per stage: one handshake per eight
   // UMMAs.
-  // The LSU variant fills one K block per stage (its loaders hand over each
-  // K block as soon as it is in shared memory).
-  static constexpr int kKSub =
-      LSU_ ? 1 : (((!PAIR_ && BN_ <= 128) || (PAIR_ && SLABS_ == 1)) ? 2 : 1);
+  static constexpr int kKSub = ((!PAIR_ && BN_ <= 128) || (PAIR_ && SLABS_ == 1)) ? 2 : 1;
   static constexpr int kABlk = kCtaRows * BK * 2;       // A of one K block
   static constexpr int kABytes = kABlk * kKSub;
   // B boxes: N-major B as 64(N) x 64(K) boxes of 8 KiB; K-major B as one box
@@ -144,15 +141,12 @@ struct TcCfg {
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
   static_assert(kTmemCols <= 512, "TMEM columns");
   static_assert(kEpiChunks >= 1, "epilogue chunking");
-  static_assert(!kLsu || (!kPair && kSlabs == 1), "per-thread operand loads: single-CTA tiles");
-  // Per-thread loads: one K block = 128 A rows (K-major) plus BN B columns,
-  // in row segments of 64 halves, 8 lanes (16-byte chunks) per segment.
+  static_assert(!kLsu || (!kPair && kSlabs == 1 && BN <= 128),
+                "per-thread operand loads: the 128 x 64 and 128 x 128 tiles");
+  // Per-thread loads: one K block = 128 A row segments (K-major) plus BN B
+  // segments of 64 halves, one segment per loader thread.
   static constexpr int kLsuThreads = 32 * kEpiWarps;
-  static constexpr int kLsuChunksA = 128 * 8;
-  static constexpr int kLsuChunks = kLsuChunksA + BN * 8;
-  static constexpr int kLsuPer = kLsuChunks / kLsuThreads;  // chunks per thread per K block
-  static_assert(kLsuChunks % kLsuThreads == 0 && kLsuChunksA % kLsuThreads == 0,
-                "whole chunks per loader thread");
+  static_assert(!kLsu || 128 + BN <= kLsuThreads, "one segment per loader thread");
 };
 
 struct TcParams {
@@ -178,6 +172,9 @@ struct TcParams {
   const half* A;
   const half* B;
   long long lda, ldb;
+  // Failure-detection self test only (gemm_selftest_stall): no operand is ever
+  // loaded, so the bounded waits of the UMMA issuer and the epilogue run out.
+  int stall;
 };
 
 // ---------------------------------------------------------------------------
@@ -192,73 +189,44 @@ struct TcParams {
 // 16-byte aligned). Elements outside the matrix read as zero, as TMA's
 // out-of-bounds fill does.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-struct LsuSeg {
-  const uint4* line;  // aligned line holding the segment's first element
-  int phase;          // the first element's position in that line (halves, 0..7)
-  int valid;          // columns of the segment inside the matrix (0..64)
-};
-
-__device__ __forceinline__ LsuSeg lsu_seg(const half* base, long long ld, int rows, int cols, int row,
-                                          int col0) {
-  LsuSeg s;
-  const bool in = row < rows && col0 < cols;
-  s.valid = in ? min(64, cols - col0) : 0;
-  const uintptr_t a0 =
-      reinterpret_cast<uintptr_t>(base + (in ? static_cast<long long>(row) * ld + col0 : 0));
-  s.phase = static_cast<int>((a0 >> 1) & 7u);
-  s.line = reinterpret_cast<const uint4*>(a0 & ~static_cast<uintptr_t>(15));
-  return s;
-}
-
-// Issue this lane's loads of segment `s` (chunk c = lane & 7): its own line and,
-// for chunk 7, the line after it.
-__device__ __forceinline__ void lsu_issue(const LsuSeg& s, int c, uint4& v, uint4& x) {
-  v = make_uint4(0, 0, 0, 0);
-  x = make_uint4(0, 0, 0, 0);
-  if (s.valid > 0 && 8 * c - s.phase < s.valid) v = ldg_nc_v4(s.line + c);
-  if (c == 7 && s.valid > 64 - s.phase) x = ldg_nc_v4(s.line + 8);
-}
-
-// Assemble this lane's chunk from its line and the next one (every lane of the
-// warp must call it: shuffles), zeroing elements outside the matrix.
-__device__ __forceinline__ uint4 lsu_assemble(const LsuSeg& s, int c, const uint4& v, const uint4& x) {
-  uint4 nx;
-  nx.x = __shfl_down_sync(0xffffffffu, v.x, 1, 8);
-  nx.y = __shfl_down_sync(0xffffffffu, v.y, 1, 8);
-  nx.z = __shfl_down_sync(0xffffffffu, v.z, 1, 8);
-  nx.w = __shfl_down_sync(0xffffffffu, v.w, 1, 8);
-  if (c == 7) nx = x;
-  const uint32_t w[8] = {v.x, v.y, v.z, v.w, nx.x, nx.y, nx.z, nx.w};
-  // halves [phase, phase + 8) of the 16 in w: whole words selected by phase / 2
-  // (two select steps), then a half-word shift when the phase is odd
-  const int q = s.phase >> 1;
-  uint32_t t[5];
+// One 64-half row segment, owned by one thread: the 9 aligned 16-byte lines
+// it touches are loaded (only lines holding elements of the matrix), then the
+// 32 words of the segment are taken from the 36 loaded words at the
+// segment's phase (halves 0..7 into the first line): two select steps move
+// by phase / 2 words, one byte permute per word moves by an odd half.
+// Elements outside the matrix come out as zero.
+__device__ __forceinline__ void lsu_segment_load(const uint4* line, int phase, int valid,
+                                                 uint4 (&w)[9]) {
 #pragma unroll
-  for (int j = 0; j < 5; ++j) {
-    const uint32_t lo = (q & 1) ? w[j + 1] : w[j];
-    const uint32_t hi = (q & 1) ? w[j + 3] : w[j + 2];
-    t[j] = (q & 2) ? hi : lo;
+  for (int i = 0; i < 9; ++i) {
+    w[i] = make_uint4(0, 0, 0, 0);
+    if (valid > 0 && 8 * i - phase < valid) w[i] = __ldg(line + i);
   }
-  uint32_t o[4];
+}
+
+__device__ __forceinline__ void lsu_segment_shift(const uint4 (&in)[9], int phase, int valid,
+                                                  uint32_t (&out)[32]) {
+  uint32_t w[36];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) o[j] = (s.phase & 1) ? __byte_perm(t[j], t[j + 1], 0x5432) : t[j];
-  const int vc = s.valid - 8 * c;  // valid elements of this chunk
-  if (vc < 8) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t keep = (2 * j < vc ? 0x0000FFFFu : 0u) | (2 * j + 1 < vc ? 0xFFFF0000u : 0u);
-      o[j] &= keep;
-    }
+  for (int i = 0; i < 9; ++i) {
+    w[4 * i] = in[i].x;
+    w[4 * i + 1] = in[i].y;
+    w[4 * i + 2] = in[i].z;
+    w[4 * i + 3] = in[i].w;
   }
-  return make_uint4(o[0], o[1], o[2], o[3]);
+  const int q = phase >> 1;
+#pragma unroll
+  for (int i = 0; i < 34; ++i) w[i] = (q & 2) ? w[i + 2] : w[i];
+#pragma unroll
+  for (int i = 0; i < 33; ++i) w[i] = (q & 1) ? w[i + 1] : w[i];
+  const uint32_t sel = (phase & 1) ? 0x5432u : 0x3210u;
+#pragma unroll
+  for (int o = 0; o < 32; ++o) out[o] = __byte_perm(w[o], w[o + 1], sel);
+  if (valid < 64) {
+#pragma unroll
+    for (int o = 0; o < 32; ++o)
+      out[o] &= (2 * o < valid ? 0x0000FFFFu : 0u) | (2 * o + 1 < valid ? 0xFFFF0000u : 0u);
+  }
 }
 
 // Grouped raster over output tiles so that concurrently resident CTAs share A
@@ -353,23 +321,22 @@ __device__ __forceinline__ void epilogue_chunk_lsu(const TcParams& p, float* til
     // lane -> column; each store instruction one contiguous 64-byte run
     const int col = col0 + lane;
     if (col < p.N) {
-      // rows in groups of 8: eight loads in flight per round trip, few registers
-#pragma unroll 1
-      for (int r0 = 0; r0 < 32; r0 += 8) {
-        float prev[8];
+      // all 32 rows' C in flight at once (the caller holds only this chunk's
+      // accumulators, so the registers are free)
+      unsigned short prev[32];
 #pragma unroll
-        for (int rr = 0; rr < 8; ++rr) {
-          const int row = row_base + r0 + rr;
-          prev[rr] = (read_c && row < p.M) ? __half2float(p.C[static_cast<size_t>(row) * p.ldc + col])
-                                           : 0.0f;
-        }
+      for (int rr = 0; rr < 32; ++rr) {
+        const int row = row_base + rr;
+        prev[rr] = (read_c && row < p.M)
+                       ? __half_as_ushort(p.C[static_cast<size_t>(row) * p.ldc + col])
+                       : static_cast<unsigned short>(0);
+      }
 #pragma unroll
-        for (int rr = 0; rr < 8; ++rr) {
-          const int row = row_base + r0 + rr;
-          if (row < p.M)
-            p.C[static_cast<size_t>(row) * p.ldc + col] =
-                __float2half_rn(fmaf(p.alpha, tile[(r0 + rr) * LD + lane], p.beta * prev[rr]));
-        }
+      for (int rr = 0; rr < 32; ++rr) {
+        const int row = row_base + rr;
+        if (row < p.M)
+          p.C[static_cast<size_t>(row) * p.ldc + col] = __float2half_rn(
+              fmaf(p.alpha, tile[rr * LD + lane], p.beta * half_bits_to_float(prev[rr])));
       }
     }
   }
@@ -561,7 +528,7 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N, LSU>::kThr
     // and, for that tile, two idle warps; they hand registers to the epilogue.
     if constexpr (SLAB_N) setmaxnreg_dec<Cfg::kRegsCtl>();
     if (warp == 0) {
-      if (!LSU && lane == 0) {
+      if (!LSU && lane == 0 && !p.stall) {
         // ---------------- TMA producer (every CTA) ----------------
         int stage = 0;
         uint32_t phase = 0;
@@ -866,8 +833,10 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N, LSU>::kThr
       // beta != 0 each buffer's C-load barrier completes once per use.
       uint32_t ctr = 0;
       uint32_t cwait[2] = {0u, 0u};
+      uint32_t cissued[2] = {0u, 0u};  // C loads issued per buffer (lane 0)
       auto issue_c_load = [&](uint32_t chunk_index, int col, int row) {
         const uint32_t b = chunk_index & 1u;
+        ++cissued[b];
         mbar_arrive_expect_tx(cload_bar(ew, b), Cfg::kEpiBufBytes);
         tma_load_2d<false>(buf0 + b * Cfg::kEpiBufBytes, &tmap_c, cload_bar(ew, b), col, row);
       };
@@ -883,78 +852,91 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N, LSU>::kThr
         int tm, tn;
         tile_coords(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
         if constexpr (LSU) {
-          // Chunk u of this thread is segment (tid + kLsuThreads * u) / 8, lane c
-          // of its 8; its address, line phase, valid columns and place in the
-          // stage are recomputed from (u, kb) when needed (registers hold only
-          // the loaded lines). A segment's line phase is the same in every K
-          // block: a K block advances it by 64 halves = 8 lines (A, Bt) or by
-          // 64 rows of B.
-          constexpr int kPer = Cfg::kLsuPer;
-          const int tid = threadIdx.x - 32 * Cfg::kEpiWarp0;  // 0 .. kLsuThreads-1
-          const int c = lane & 7;
-          const int m0 = tm * Cfg::kTileM;
-          const int n0 = tn * Cfg::kTileN;
-          auto geom = [&](int u, int kb, LsuSeg& g) {
-            const int r = (tid + Cfg::kLsuThreads * u) >> 3;
-            const int kx = kb * Cfg::BK;
-            if (r < 128) {
-              g = lsu_seg(p.A, p.lda, p.M, p.K, m0 + r, kx);
+          if (!p.stall) {
+            // Loader thread t owns one 64-half row segment in every K block:
+            // A row m0 + t (t < 128); then for B[K,N] the K row 64 kb + kk of
+            // column box j (t - 128 = 64 j + kk), for Bt[N,K] the row n0 + t - 128.
+            // The segment's position in its 16-byte line is the same in every K
+            // block (a K block moves it by 64 halves or 64 rows), and its 8
+            // chunks land in one 128-byte row of the 128B-swizzled stage (chunk c
+            // at c ^ (row % 8): 32 lanes' stores are conflict-free). Loads of the
+            // next K block are in flight while this one is shifted and stored.
+            const int t = threadIdx.x - 32 * Cfg::kEpiWarp0;  // 0 .. kLsuThreads-1
+            const bool is_a = t < 128;
+            const bool active = t < 128 + BN;
+            const int m0 = tm * Cfg::kTileM;
+            const int n0 = tn * Cfg::kTileN;
+            const int rb = t - 128;
+            uint64_t base;   // byte address of the segment's first element in K block 0
+            uint64_t step;   // bytes per K block
+            int srow;        // row of the segment in its 128-byte-row stage layout
+            uint32_t soff;   // offset of that row in the stage region (A or B)
+            if (is_a) {
+              base = reinterpret_cast<uint64_t>(p.A) +
+                     2ull * static_cast<uint64_t>(m0 + t) * static_cast<uint64_t>(p.lda);
+              step = 128;
+              srow = t;
+              soff = static_cast<uint32_t>(t * 128);
             } else if constexpr (BKM) {
-              g = lsu_seg(p.B, p.ldb, p.N, p.K, n0 + r - 128, kx);
+              base = reinterpret_cast<uint64_t>(p.B) +
+                     2ull * static_cast<uint64_t>(n0 + rb) * static_cast<uint64_t>(p.ldb);
+              step = 128;
+              srow = rb;
+              soff = static_cast<uint32_t>(rb * 128);
             } else {
-              const int rb = r - 128;
-              g = lsu_seg(p.B, p.ldb, p.K, p.N, kx + (rb & 63), n0 + 64 * (rb >> 6));
+              const int j = rb >> 6, kk = rb & 63;
+              base = reinterpret_cast<uint64_t>(p.B) +
+                     2ull * (static_cast<uint64_t>(kk) * static_cast<uint64_t>(p.ldb) + n0 + 64 * j);
+              step = 128ull * static_cast<uint64_t>(p.ldb);
+              srow = kk;
+              soff = static_cast<uint32_t>(j * Cfg::kBBoxBytes + kk * 128);
             }
-          };
-          // the chunk's 16 bytes in the stage (128B swizzle: 16-byte unit c of a
-          // 128-byte row lands at c ^ (row % 8))
-          auto doff = [&](int u, uint32_t sa, uint32_t sb) {
-            const int r = (tid + Cfg::kLsuThreads * u) >> 3;
-            if (r < 128) return sa + static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
-            const int rb = r - 128;
-            if constexpr (BKM) return sb + static_cast<uint32_t>(rb * 128 + ((c ^ (rb & 7)) << 4));
-            const int kk = rb & 63;
-            return sb + static_cast<uint32_t>((rb >> 6) * Cfg::kBBoxBytes + kk * 128 +
-                                              ((c ^ (kk & 7)) << 4));
-          };
-          uint4 v[kPer], x[kPer];
-          if (kb_lo < kb_hi) {
-#pragma unroll
-            for (int u = 0; u < kPer; ++u) {
-              LsuSeg g;
-              geom(u, kb_lo, g);
-              lsu_issue(g, c, v[u], x[u]);
-            }
-          }
-          for (int kb = kb_lo; kb < kb_hi; ++kb) {
-            // registers may be loaded early; the stage must be free before it is written
-            if (!mbar_wait_warp(empty_bar(ld_stage), ld_phase ^ 1u, p.timeout_ns, abort_flag, p.err,
-                                kErrTimeoutProducer)) {
-              ok = false;
-              break;
-            }
-            const uint32_t sa = sA0 + ld_stage * Cfg::kABytes;
-            const uint32_t sb = sB0 + ld_stage * Cfg::kBBytes;
-            const bool more = kb + 1 < kb_hi;
-#pragma unroll
-            for (int u = 0; u < kPer; ++u) {
-              LsuSeg g;
-              geom(u, kb, g);
-              st_shared_v4(doff(u, sa, sb), lsu_assemble(g, c, v[u], x[u]));
-              // this chunk's loads for the next K block go out while the rest
-              // of this one is assembled
-              if (more) {
-                geom(u, kb + 1, g);
-                lsu_issue(g, c, v[u], x[u]);
+            const int phase = static_cast<int>((base >> 1) & 7u);
+            const int b_cols = max(0, min(64, p.N - n0 - 64 * (rb >> 6)));  // B[K,N] boxes
+            auto seg_valid = [&](int kb) -> int {
+              const int kx = kb * Cfg::BK;
+              if (!active) return 0;
+              if (is_a) return m0 + t < p.M ? min(64, p.K - kx) : 0;
+              if constexpr (BKM) return n0 + rb < p.N ? min(64, p.K - kx) : 0;
+              return kx + (rb & 63) < p.K ? b_cols : 0;
+            };
+            auto seg_line = [&](int kb) {
+              return reinterpret_cast<const uint4*>((base + static_cast<uint64_t>(kb) * step) & ~15ull);
+            };
+            uint8_t* const region = smem + ((is_a ? sA0 : sB0) - sbase) + soff;
+            const int region_stage = is_a ? Cfg::kABytes : Cfg::kBBytes;
+            const int region_kb = is_a ? Cfg::kABlk : Cfg::kBBlk;
+            uint4 w[9];
+            if (kb_lo < kb_hi) lsu_segment_load(seg_line(kb_lo), phase, seg_valid(kb_lo), w);
+            for (int kb0 = kb_lo; kb0 < kb_hi && ok; kb0 += Cfg::kKSub) {
+              // registers may be loaded early; the stage must be free before it is written
+              if (!mbar_wait_warp(empty_bar(ld_stage), ld_phase ^ 1u, p.timeout_ns, abort_flag, p.err,
+                                  kErrTimeoutProducer)) {
+                ok = false;
+                break;
               }
-            }
-            // generic-proxy writes -> visible to the tensor core (async proxy)
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(full_bar(ld_stage));
-            if (++ld_stage == kStages) {
-              ld_stage = 0;
-              ld_phase ^= 1u;
+              const int nsub = min(Cfg::kKSub, kb_hi - kb0);
+              for (int q = 0; q < nsub; ++q) {
+                const int kb = kb0 + q;
+                uint32_t o[32];
+                lsu_segment_shift(w, phase, seg_valid(kb), o);
+                if (kb + 1 < kb_hi) lsu_segment_load(seg_line(kb + 1), phase, seg_valid(kb + 1), w);
+                if (active) {
+                  uint8_t* dst = region + ld_stage * region_stage + q * region_kb;
+  #pragma unroll
+                  for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<uint4*>(dst + ((c ^ (srow & 7)) << 4)) =
+                        make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                }
+              }
+              // generic-proxy writes -> visible to the tensor core (async proxy)
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(full_bar(ld_stage));
+              if (++ld_stage == kStages) {
+                ld_stage = 0;
+                ld_phase ^= 1u;
+              }
             }
           }
           if (!ok) break;
@@ -995,6 +977,31 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N, LSU>::kThr
               for (int j = 0; j < 8; ++j)
                 dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
                                      __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            }
+            continue;
+          }
+          if (!p.c_tma) {
+            // C that TMA cannot address: one 32-column chunk at a time out of
+            // TMEM, through the transposed smem tile, to C (only one chunk of
+            // accumulators live, so every C load of the chunk can be in
+            // flight together); TMEM is handed back after the last chunk.
+            const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                    static_cast<uint32_t>(acc * Cfg::kAccCols + sl * BN +
+                                                          col_half * Cfg::kEpiCols);
+  #pragma unroll 1
+            for (int c = 0; c < kChunks; ++c) {
+              uint32_t r[32];
+              tmem_ld_32x32b_x32(t_addr + c * 32, r);
+              tmem_wait_ld();
+              epilogue_chunk_lsu(p, lsu_tile, row_base, col_base + c * Cfg::kEpiChunk, r, lane);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if (PAIR && !leader)
+                mbar_arrive_remote_signal(mapa_shared(tempty_bar(acc, sl), pbase));
+              else
+                mbar_arrive(tempty_bar(acc, sl));
             }
             continue;
           }
@@ -1066,8 +1073,6 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N, LSU>::kThr
                   issue_c_load(ctr + 2, col0 + 2 * Cfg::kEpiChunk, row_base);
                 }
               }
-            } else {
-              epilogue_chunk_lsu(p, lsu_tile, row_base, col0, &r[32 * c], lane);
             }
             ++ctr;
           }
@@ -1076,6 +1081,15 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N, LSU>::kThr
           acc = 0;
           acc_phase ^= 1u;
         }
+      }
+      if (!ok && lane == 0) {
+        // unwinding after a wait ran out: C boxes already requested land in
+        // this CTA's shared memory, so wait for them (bounded) before leaving
+        volatile int no_abort = 0;
+        for (int b = 0; b < 2; ++b)
+          for (; cwait[b] < cissued[b]; ++cwait[b])
+            mbar_wait(cload_bar(ew, b), cwait[b] & 1u, p.timeout_ns, &no_abort, p.err,
+                      kErrTimeoutEpilogue);
       }
       if (lane == 0) bulk_wait_all();  // every TMA store of this warp has landed
     }
@@ -1088,16 +1102,24 @@ __global__ void __launch_bounds__(TcCfg<BN, PAIR, BKM, SLABS, SLAB_N, LSU>::kThr
     // partial of the same tile; CTA q of them reduces slice q of the rows.
     cluster_sync_all();  // all partials written and visible
     if constexpr (Cfg::kSplitK) {
+      // A CTA of the cluster whose waits ran out has no valid partial: then no
+      // CTA of the cluster writes C (the status carries the error).
+      bool any_abort = false;
+      for (int k = 0; k < p.ksplit; ++k)
+        any_abort |= __float_as_int(ld_shared_cluster_f32(mapa_shared(
+                         smem_u32(const_cast<int*>(abort_flag)), static_cast<uint32_t>(k)))) != 0;
       const int q = static_cast<int>(cluster_ctarank());
       int tm, tn;
       tile_coords(unit, p.tiles_m, p.tiles_n, p.group, tm, tn);
       const int row0 = tm * Cfg::kTileM;
       const int col0 = tn * Cfg::kTileN;
       const uint32_t part = smem_u32(smem);
-      switch (p.ksplit) {
-        case 2: splitk_reduce<2, BN>(p, part, q, row0, col0); break;
-        case 4: splitk_reduce<4, BN>(p, part, q, row0, col0); break;
-        default: splitk_reduce<8, BN>(p, part, q, row0, col0); break;
+      if (!any_abort) {
+        switch (p.ksplit) {
+          case 2: splitk_reduce<2, BN>(p, part, q, row0, col0); break;
+          case 4: splitk_reduce<4, BN>(p, part, q, row0, col0); break;
+          default: splitk_reduce<8, BN>(p, part, q, row0, col0); break;
+        }
       }
     }
     cluster_sync_all();  // peers may still be reading this CTA's partial

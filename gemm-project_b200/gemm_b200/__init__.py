@@ -56,6 +56,8 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gemm_launch_error.restype = i
     lib.gemm_launcher_sub.argtypes = [vp, i, vp, i, vp, i, i, i, i, f, f, vp, i]
     lib.gemm_launcher_sub.restype = i
+    lib.gemm_selftest_stall.argtypes = [vp, vp, vp, i, i, i, i, i, i, vp]
+    lib.gemm_selftest_stall.restype = i
     return lib
 
 

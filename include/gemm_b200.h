@@ -57,7 +57,10 @@ GEMM_API void gemm_launcher_stream(const gemm_half_t* A, const gemm_half_t* B, g
  * 4 = multi-row kernel with per-thread loads, 5 = column kernel with
  * per-thread loads (the paths misaligned operands take), 6 = small-M
  * tensor-core kernel (M <= 256, 16-byte aligned A and B, K % 8 == 0, N % 8 == 0).
- * tile_n (path 1): 0 = automatic; 64, 128 or 256 = one CTA per 128 x tile_n
+ * 7 = the tcgen05 tile kernel reading A and B with per-thread loads at any
+ * alignment and pitch (no repack; what path 1 uses for misaligned operands of
+ * problems up to 3.5e10 FLOPs; tiles 128 x 64 and 128 x 128).
+ * tile_n (paths 1 and 7): 0 = automatic; 64, 128 or 256 = one CTA per 128 x tile_n
  * output tile (tcgen05.mma.cta_group::1); 2 = a 2-CTA cluster per 256 x 256
  * output tile (tcgen05.mma.cta_group::2); 3 = a 2-CTA cluster per 512 x 256
  * output tile (two 128-row A slabs per CTA); 4 = a 2-CTA cluster per 256 x 512
@@ -123,13 +126,19 @@ GEMM_API int gemm_launch_error(void);
  * A's or B's base is not 16-byte aligned, or K or N is not a multiple of 8, and
  * the shape goes to the tensor-core kernel) is not an option.
  * This entry point never calls cudaMalloc, cudaMallocAsync, cudaFree or any
- * allocating library routine. The repack uses one fixed 32 MiB device buffer
- * that is part of the library image: every GPU that loads the library holds
- * it until the process exits. The first call on a device looks up that
- * buffer's device address, so make the first call on each device before any
- * stream capture. All calls share the buffer: calls that overlap on the GPU
- * (other streams, other host threads) race on it and must be serialized by the
- * caller. Shapes that need no repack run exactly as gemm_launcher_stream.
+ * allocating library routine. It makes the same plan as gemm_launcher_stream
+ * (kernel, tile, K split: the results are bit-identical); where that plan
+ * takes repack scratch from the library's pool (misaligned operands of a
+ * problem too large for the in-place loads), the repack uses one fixed 32 MiB
+ * device buffer that is part of the library image instead: every GPU that
+ * loads the library holds it until the process exits. The buffer is committed
+ * when the library's module loads on a device, which under CUDA's default lazy
+ * module loading is the library's first call there, so make one call on each
+ * device before reserving the rest of its memory. The first call on a device
+ * also looks up the buffer's device address, so make it before any stream
+ * capture. All calls share the buffer: calls that overlap on the GPU (other
+ * streams, other host threads) race on it and must be serialized by the
+ * caller. Every other call runs exactly as gemm_launcher_stream.
  * Returns 0 on success; -2 if the repack would need more than 32 MiB
  * (M*roundup8(K)*2 rounded up to 256, plus K*roundup8(N)*2 bytes; nothing is
  * launched and C is untouched; a message goes to stderr); -1 if the buffer's
@@ -143,7 +152,7 @@ GEMM_API int gemm_launcher_noalloc(const gemm_half_t* A, const gemm_half_t* B, g
  * every call since the last query launched and no kernel reported an error,
  * a cudaError_t value (1..999) for the first failed launch on this thread, or
  * 1000 + code for a device-side bounded wait that ran out
- * (1001 producer, 1002 MMA issuer, 1003 epilogue, 1005 wait probe).
+ * (1001 operand producer or loader, 1002 MMA issuer, 1003 epilogue, 1005 wait probe).
  * Reading the device word synchronizes with the legacy default stream.
  * The status is cleared by the call. */
 GEMM_API int gemm_launcher_status(void);
@@ -174,6 +183,19 @@ GEMM_API int gemm_slab_rows(int M, int world, int rank, int* row0);
  * and returns instead of hanging; the call synchronizes the stream and returns
  * gemm_launcher_status() (1005 when the bound worked). */
 GEMM_API int gemm_selftest_wait_timeout(int timeout_us, cudaStream_t stream);
+
+/* Failure-detection self test on the real tile kernel (no counterpart in the
+ * reference): runs the dense tcgen05 kernel that gemm_launcher_ex would run for
+ * this shape (path 1, or 7 for the variant with per-thread operand loads;
+ * tile_n as for gemm_launcher_ex) with alpha = 1, beta = 0 and its operand
+ * feed switched off: no load of A or B is issued, so the UMMA issuer's and
+ * the epilogue's bounded waits run out after timeout_us microseconds, the
+ * kernel records its code, unwinds, frees its TMEM and returns. C is not
+ * written. Synchronizes `stream` and returns gemm_launcher_status() (1001,
+ * 1002 or 1003 when the bound worked), or -1 for arguments it cannot run. */
+GEMM_API int gemm_selftest_stall(const gemm_half_t* A, const gemm_half_t* B, gemm_half_t* C,
+                                 int M, int N, int K, int path, int tile_n, int timeout_us,
+                                 cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -61,14 +61,14 @@ def test_tc_path(lib, cuda, shape, tile_n):
 
 
 # The tile kernel with per-thread operand loads (path 7: A and B read in place at
-# any alignment and pitch, no repack): every single-CTA tile, ragged M/N/K, each
+# any alignment and pitch, no repack): both of its tiles, ragged M/N/K, each
 # pointer at half offsets 0, 1 and 3 (phases of the 16-byte lines), K and N that
 # are not multiples of 8 (rows of alternating phase), beta = 0 over NaN C.
 LSU_SHAPES = [(128, 256, 64), (129, 257, 65), (1023, 2049, 777), (300, 1000, 72), (17, 19, 23),
               (513, 264, 200), (640, 384, 4104), (1000, 2056, 136), (256, 130, 1031)]
 
 
-@pytest.mark.parametrize("tile_n", [64, 128, 256], ids=["128x64", "128x128", "128x256"])
+@pytest.mark.parametrize("tile_n", [64, 128], ids=["128x64", "128x128"])
 @pytest.mark.parametrize("shape", LSU_SHAPES, ids=str)
 @pytest.mark.parametrize("offsets", [(0, 0, 0), (1, 1, 1), (3, 1, 0), (0, 3, 1)], ids=str)
 def test_tc_lsu_path(lib, cuda, shape, tile_n, offsets):
@@ -78,7 +78,7 @@ def test_tc_lsu_path(lib, cuda, shape, tile_n, offsets):
         offsets=offsets, seed=m + n + k + sum(offsets))
 
 
-@pytest.mark.parametrize("tile,ks", [(64, 4), (128, 2), (128, 8), (256, 4)], ids=str)
+@pytest.mark.parametrize("tile,ks", [(64, 4), (64, 8), (128, 2), (128, 4), (128, 8)], ids=str)
 def test_tc_lsu_split_k(lib, cuda, monkeypatch, tile, ks):
     monkeypatch.setenv("GEMM_SPLITK_TILE", str(tile))
     monkeypatch.setenv("GEMM_SPLITK_KS", str(ks))
