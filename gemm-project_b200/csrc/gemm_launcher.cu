@@ -78,7 +78,7 @@ struct DeviceInfo {
   int dec_slots[5] = {0, 0, 0, 0, 0};  // co-resident CTAs of skinny_tc_kernel<16|32|64|128|256>
   int split_clusters[3] = {0, 0, 0};   // co-resident (1, ks) split-K clusters, ks = 2, 4, 8
   int* err = nullptr;
-  cudaMemPool_t pool = nullptr;   // repack scratch (never trimmed between calls)
+  cudaMemPool_t pool = nullptr;   // repack scratch (keeps up to 64 MiB between calls)
   std::atomic<bool> configured{false};
 };
 DeviceInfo g_dev[kMaxDevices];
@@ -282,7 +282,11 @@ DeviceInfo& device_info() {
       props.location.type = cudaMemLocationTypeDevice;
       props.location.id = dev;
       if (cudaMemPoolCreate(&d.pool, &props) == cudaSuccess) {
-        uint64_t keep = ~uint64_t(0);
+        // keep up to 64 MiB of repack scratch across synchronizations (steady
+        // state reuses it without new device allocations); anything above is
+        // returned to the system at the next synchronization, so one large
+        // misaligned call does not hold its scratch for the life of the process
+        uint64_t keep = uint64_t(64) << 20;
         cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep);
       } else {
         cudaGetLastError();
@@ -640,11 +644,36 @@ size_t repack_bytes(const half* A, const half* B, int M, int N, int K) {
   return (a_bytes + 255) / 256 * 256 + b_bytes;
 }
 
+// One launch of pack_rows_kernel for up to two operands (jobs with rows == 0
+// are empty), as a programmatic dependent of the previous kernel in the stream
+// when PDL is on. `names` is the launch-log spelling for A, B and both.
+void launch_pack(const PackJob& j0, const PackJob& j1, const char* name, int M, int N, int K,
+                 cudaStream_t s, const DeviceInfo& d) {
+  const int threads = 256;
+  const size_t work = static_cast<size_t>(j0.rows) * ceil_div(j0.cols, 8) +
+                      static_cast<size_t>(j1.rows) * ceil_div(j1.cols, 8);
+  const int blocks =
+      static_cast<int>(std::max<size_t>(1, std::min<size_t>((work + threads - 1) / threads,
+                                                             size_t(d.sms) * 16)));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(blocks, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  log_launch(name, M, N, K, cfg.gridDim, cfg.blockDim);
+  record_error(cudaLaunchKernelEx(&cfg, pack_rows_kernel, j0, j1));
+}
+
 // Copy whichever of A and B is not TMA-addressable into `scratch` (laid out as
-// repack_bytes() describes) with its pitch rounded up to 8 halves, and point
-// a_src/b_src (pitches lda/ldb) at the operands the kernel should read.
+// repack_bytes() describes) with its pitch rounded up to 8 halves, in one
+// launch, and point a_src/b_src (pitches lda/ldb) at the operands the kernel
+// should read. names: launch-log spellings for A only, B only, both.
 void repack_operands(const half* A, const half* B, int M, int N, int K, cudaStream_t s,
-                     const DeviceInfo& d, void* scratch, const char* const names[2],
+                     const DeviceInfo& d, void* scratch, const char* const names[3],
                      const half** a_src, int* lda, const half** b_src, int* ldb) {
   const bool a_ok = aligned16(A) && K % 8 == 0;
   const bool b_ok = aligned16(B) && N % 8 == 0;
@@ -654,25 +683,18 @@ void repack_operands(const half* A, const half* B, int M, int N, int K, cudaStre
   *ldb = N;
   size_t a_bytes = a_ok ? 0 : static_cast<size_t>(M) * round_up8(K) * sizeof(half);
   a_bytes = (a_bytes + 255) / 256 * 256;
-  const int threads = 256;
+  PackJob ja{A, static_cast<half*>(scratch), static_cast<size_t>(K),
+             static_cast<size_t>(round_up8(K)), a_ok ? 0 : M, K};
+  PackJob jb{B, reinterpret_cast<half*>(static_cast<char*>(scratch) + a_bytes),
+             static_cast<size_t>(N), static_cast<size_t>(round_up8(N)), b_ok ? 0 : K, N};
+  if (a_ok && b_ok) return;
+  launch_pack(ja, jb, names[!a_ok && !b_ok ? 2 : (a_ok ? 1 : 0)], M, N, K, s, d);
   if (!a_ok) {
-    half* dst = static_cast<half*>(scratch);
-    const size_t work = static_cast<size_t>(M) * ceil_div(K, 8);
-    const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
-    log_launch(names[0], M, N, K, dim3(blocks), dim3(threads));
-    pack_rows_kernel<<<blocks, threads, 0, s>>>(A, K, dst, round_up8(K), M, K);
-    record_error(cudaGetLastError());
-    *a_src = dst;
+    *a_src = ja.dst;
     *lda = round_up8(K);
   }
   if (!b_ok) {
-    half* dst = reinterpret_cast<half*>(static_cast<char*>(scratch) + a_bytes);
-    const size_t work = static_cast<size_t>(K) * ceil_div(N, 8);
-    const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
-    log_launch(names[1], M, N, K, dim3(blocks), dim3(threads));
-    pack_rows_kernel<<<blocks, threads, 0, s>>>(B, N, dst, round_up8(N), K, N);
-    record_error(cudaGetLastError());
-    *b_src = dst;
+    *b_src = jb.dst;
     *ldb = round_up8(N);
   }
 }
@@ -683,12 +705,17 @@ void repack_operands(const half* A, const half* B, int M, int N, int K, cudaStre
 bool a_tma_ok(const half* A, int K) { return aligned16(A) && K % 8 == 0; }
 bool b_tma_ok(const half* B, int N) { return aligned16(B) && N % 8 == 0; }
 
-// Such operands are read in place by the LSU variant of the tile kernel (per-
-// thread loads into the same swizzled stages: no repack pass, no scratch), up
-// to a problem size where its slower operand feed would cost more than a
-// repack pass over A and B plus the TMA-fed kernel (measured on B200; beyond
-// it the repack path runs). GEMM_LSU=1 forces the LSU variant, -1 the repack.
-constexpr double kLsuMaxFlops = 3.5e10;
+// Such operands are either repacked into stream-ordered scratch (one launch for
+// both, then the TMA-fed kernel) or read in place by the LSU variant of the
+// tile kernel (per-thread loads into the same swizzled stages: no repack, no
+// scratch, one launch). Per-thread loads from scattered rows feed the tensor
+// core at about a quarter of TMA's rate (measured on B200: 2048^3 117 us in
+// place, 32 us repacked, device time), so the repack is faster on the device at
+// every size; the in-place variant wins per call on tiny problems, where the
+// repack's extra launch and pool bookkeeping on the host dominate (129 x 257 x
+// 65: 15 against 23 us per call). GEMM_LSU=1 forces the LSU variant, -1 the
+// repack.
+constexpr double kLsuMaxFlops = 1.0e8;
 
 bool use_lsu(int M, int N, int K) {
   const int f = env_int("GEMM_LSU");
@@ -770,11 +797,13 @@ int launch_tc_planned(const half* A, const half* B, half* C, int M, int N, int K
         record_error(e);
         return -1;
       }
-      static const char* const names[2] = {"pack_rows_kernel<A>", "pack_rows_kernel<B>"};
+      static const char* const names[3] = {"pack_rows_kernel<A>", "pack_rows_kernel<B>",
+                                           "pack_rows_kernel<A,B>"};
       repack_operands(A, B, M, N, K, s, d, pooled, names, &a_src, &lda, &b_src, &ldb);
     } else {
-      static const char* const names[2] = {"pack_rows_kernel<A,static>",
-                                           "pack_rows_kernel<B,static>"};
+      static const char* const names[3] = {"pack_rows_kernel<A,static>",
+                                           "pack_rows_kernel<B,static>",
+                                           "pack_rows_kernel<A,B,static>"};
       repack_operands(A, B, M, N, K, s, d, scratch, names, &a_src, &lda, &b_src, &ldb);
     }
   }
@@ -1175,25 +1204,20 @@ int launch_tn(const half* A, const half* Bt, half* C, int M, int N, int K, float
       record_error(e);
       return -1;
     }
-    const int threads = 256;
+    PackJob ja{A, static_cast<half*>(scratch), static_cast<size_t>(K),
+               static_cast<size_t>(round_up8(K)), a_ok ? 0 : M, K};
+    PackJob jb{Bt, reinterpret_cast<half*>(static_cast<char*>(scratch) + a_bytes),
+               static_cast<size_t>(K), static_cast<size_t>(round_up8(K)), b_ok ? 0 : N, K};
+    launch_pack(ja, jb,
+                !a_ok && !b_ok ? "pack_rows_kernel<A,Bt>"
+                               : (a_ok ? "pack_rows_kernel<Bt>" : "pack_rows_kernel<A>"),
+                M, N, K, s, d);
     if (!a_ok) {
-      half* dst = static_cast<half*>(scratch);
-      const size_t work = static_cast<size_t>(M) * ceil_div(K, 8);
-      const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
-      log_launch("pack_rows_kernel<A>", M, N, K, dim3(blocks), dim3(threads));
-      pack_rows_kernel<<<blocks, threads, 0, s>>>(A, K, dst, round_up8(K), M, K);
-      record_error(cudaGetLastError());
-      a_src = dst;
+      a_src = ja.dst;
       lda = round_up8(K);
     }
     if (!b_ok) {
-      half* dst = reinterpret_cast<half*>(static_cast<char*>(scratch) + a_bytes);
-      const size_t work = static_cast<size_t>(N) * ceil_div(K, 8);
-      const int blocks = static_cast<int>(std::min<size_t>((work + threads - 1) / threads, size_t(d.sms) * 16));
-      log_launch("pack_rows_kernel<Bt>", M, N, K, dim3(blocks), dim3(threads));
-      pack_rows_kernel<<<blocks, threads, 0, s>>>(Bt, K, dst, round_up8(K), N, K);
-      record_error(cudaGetLastError());
-      b_src = dst;
+      b_src = jb.dst;
       ldb = round_up8(K);
     }
   }

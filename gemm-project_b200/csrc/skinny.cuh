@@ -281,27 +281,47 @@ __global__ void scale_c_kernel(half* C, size_t count, float beta) {
 // a buffer with row stride `dst_ld` (16-byte aligned base, dst_ld % 8 == 0) so
 // that TMA can address it. Columns beyond `cols` are not written: the tensor
 // map declares only `cols` columns and TMA zero-fills past them.
-__global__ void pack_rows_kernel(const half* __restrict__ src, size_t src_ld, half* __restrict__ dst,
-                                 size_t dst_ld, int rows, int cols) {
-  const int groups = (cols + 7) / 8;
-  const size_t total = static_cast<size_t>(rows) * groups;
+// One operand to repack: `rows` rows of `cols` halves from src (row pitch
+// src_ld, any 2-byte alignment) to dst (row pitch dst_ld, a multiple of 8, and
+// a 16-byte aligned base), so that TMA can address the copy.
+struct PackJob {
+  const half* src;
+  half* dst;
+  size_t src_ld, dst_ld;
+  int rows, cols;
+};
+
+// Repack of up to two operands in one launch (the grid strides over the
+// 8-half groups of both). Launched as a programmatic dependent: it lets the
+// GEMM that follows start its set-up at once and waits for the kernel before
+// it (which may still write A or B) before its first load.
+__global__ void pack_rows_kernel(const PackJob j0, const PackJob j1) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int g0 = (j0.cols + 7) / 8, g1 = (j1.cols + 7) / 8;
+  const size_t n0 = static_cast<size_t>(j0.rows) * g0;
+  const size_t total = n0 + static_cast<size_t>(j1.rows) * g1;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const int r = static_cast<int>(i / groups);
-    const int c0 = static_cast<int>(i % groups) * 8;
-    const half* s = src + r * src_ld + c0;
-    half* d = dst + r * dst_ld + c0;
-    if (c0 + 8 <= cols) {
+    const bool first = i < n0;
+    const PackJob& j = first ? j0 : j1;
+    const size_t k = first ? i : i - n0;
+    const int groups = first ? g0 : g1;
+    const int r = static_cast<int>(k / groups);
+    const int c0 = static_cast<int>(k % groups) * 8;
+    const half* s = j.src + r * j.src_ld + c0;
+    half* d = j.dst + r * j.dst_ld + c0;
+    if (c0 + 8 <= j.cols) {
       uint32_t w[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t lo = __half_as_ushort(s[2 * j]);
-        const uint32_t hi = __half_as_ushort(s[2 * j + 1]);
-        w[j] = lo | (hi << 16);
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t lo = __half_as_ushort(s[2 * q]);
+        const uint32_t hi = __half_as_ushort(s[2 * q + 1]);
+        w[q] = lo | (hi << 16);
       }
       *reinterpret_cast<uint4*>(d) = make_uint4(w[0], w[1], w[2], w[3]);
     } else {
-      for (int j = 0; c0 + j < cols; ++j) d[j] = s[j];
+      for (int q = 0; c0 + q < j.cols; ++q) d[q] = s[q];
     }
   }
 }

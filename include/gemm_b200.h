@@ -58,8 +58,8 @@ GEMM_API void gemm_launcher_stream(const gemm_half_t* A, const gemm_half_t* B, g
  * per-thread loads (the paths misaligned operands take), 6 = small-M
  * tensor-core kernel (M <= 256, 16-byte aligned A and B, K % 8 == 0, N % 8 == 0).
  * 7 = the tcgen05 tile kernel reading A and B with per-thread loads at any
- * alignment and pitch (no repack; what path 1 uses for misaligned operands of
- * problems up to 3.5e10 FLOPs; tiles 128 x 64 and 128 x 128).
+ * alignment and pitch (no repack, no scratch; what path 1 uses for misaligned
+ * operands of problems up to 1e8 FLOPs; tiles 128 x 64 and 128 x 128).
  * tile_n (paths 1 and 7): 0 = automatic; 64, 128 or 256 = one CTA per 128 x tile_n
  * output tile (tcgen05.mma.cta_group::1); 2 = a 2-CTA cluster per 256 x 256
  * output tile (tcgen05.mma.cta_group::2); 3 = a 2-CTA cluster per 512 x 256
@@ -129,7 +129,7 @@ GEMM_API int gemm_launch_error(void);
  * allocating library routine. It makes the same plan as gemm_launcher_stream
  * (kernel, tile, K split: the results are bit-identical); where that plan
  * takes repack scratch from the library's pool (misaligned operands of a
- * problem too large for the in-place loads), the repack uses one fixed 32 MiB
+ * problem above 1e8 FLOPs), the repack uses one fixed 32 MiB
  * device buffer that is part of the library image instead: every GPU that
  * loads the library holds it until the process exits. The buffer is committed
  * when the library's module loads on a device, which under CUDA's default lazy

@@ -98,27 +98,42 @@ def test_misaligned_dense_both_feeds(lib, cuda, monkeypatch, lsu, shape):
     assert ("lsu" in gemm_b200.last_kernel()) == (lsu == "1"), gemm_b200.last_kernel()
 
 
-def test_misaligned_dense_allocates_nothing(lib, cuda):
-    """The reference's misaligned dense config through gemm_launcher: one kernel,
-    operands read in place, so no call takes device memory (free memory is
-    unchanged across 100 calls that start from a fresh shape)."""
-    import gemm_b200
-    m, n, k = 1023, 2049, 777
+def _misaligned_calls(lib, cuda, m, n, k, calls):
+    """free device memory before the first and after the last of `calls`
+    gemm_launcher calls on operands offset by one half (fresh buffers)."""
     ga = Guarded((m, k), cuda, fill=0.5, offset=65)
     gb = Guarded((k, n), cuda, fill=0.25, offset=65)
     gc = Guarded((m, n), cuda, fill=1.0, offset=65)
     f = ctypes.c_float
     torch.cuda.synchronize()
     free0, _ = torch.cuda.mem_get_info()
-    for _ in range(100):
+    for _ in range(calls):
         lib.gemm_launcher(ga.tensor.data_ptr(), gb.tensor.data_ptr(), gc.tensor.data_ptr(), m, n, k,
                           f(0.75), f(-0.25))
     torch.cuda.synchronize()
     free1, _ = torch.cuda.mem_get_info()
-    assert lib.gemm_launcher_status() == 0
+    assert lib.gemm_launcher_status() == 0 and gc.canaries_ok()
+    return free0, free1
+
+
+def test_tiny_misaligned_dense_allocates_nothing(lib, cuda):
+    """Tiny misaligned problems are read in place by the tile kernel: not even
+    the first call takes device memory."""
+    import gemm_b200
+    free0, free1 = _misaligned_calls(lib, cuda, 129, 257, 65, 100)
     assert "lsu" in gemm_b200.last_kernel()
     assert free1 == free0, f"free device memory moved by {free0 - free1} bytes"
-    assert gc.canaries_ok()
+
+
+def test_misaligned_dense_steady_state_allocates_nothing(lib, cuda):
+    """The reference's misaligned dense config through gemm_launcher: the repack
+    scratch comes from the library's pool, so after the first call 100 more take
+    no further device memory."""
+    import gemm_b200
+    _misaligned_calls(lib, cuda, 1023, 2049, 777, 1)
+    free0, free1 = _misaligned_calls(lib, cuda, 1023, 2049, 777, 100)
+    assert gemm_b200.last_kernel() == "tc_gemm_kernel<128x128>"
+    assert free1 == free0, f"free device memory moved by {free0 - free1} bytes"
 
 
 # Cluster split-K on 128 x 256 tiles (tile code 5): ragged M, N and K, the

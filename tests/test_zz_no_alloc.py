@@ -135,9 +135,9 @@ def test_noalloc_uses_fixed_buffer_in_fresh_process(lib, cuda):
                           text=True, env=env, timeout=300)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
     out = proc.stdout
-    assert "pack_rows_kernel<A,static>: M=2000 N=2056 K=3001" in out, out[-3000:]
-    assert "pack_rows_kernel<B,static>: M=1500 N=3000 K=2049" in out, out[-3000:]
-    assert "pack_rows_kernel<A>:" not in out and "pack_rows_kernel<B>:" not in out
+    assert "pack_rows_kernel<A,B,static>: M=2000 N=2056 K=3001" in out, out[-3000:]
+    assert "pack_rows_kernel<A,B,static>: M=1500 N=3000 K=2049" in out, out[-3000:]
+    assert "pack_rows_kernel<A,B>:" not in out and "pack_rows_kernel<A>:" not in out
     delta = [int(ln.split()[1]) for ln in out.splitlines() if ln.startswith("FREE_DELTA")]
     assert delta == [0], out[-2000:]
 
