@@ -527,7 +527,10 @@ void launch_tc_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   } else {
     cfg.gridDim = dim3(std::min(tiles, max_sms > 0 ? std::min(d.sms, max_sms) : d.sms), 1, 1);
   }
-  if (pdl_enabled()) {
+  // No programmatic launch under an SM cap: a dependent kernel's CTAs would
+  // start early and wait (holding a whole SM's shared memory each) on exactly
+  // the SMs the cap leaves free for concurrent work such as NCCL's kernels.
+  if (pdl_enabled() && max_sms <= 0) {
     attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
