@@ -87,10 +87,19 @@ struct TcCfg {
   static constexpr int kSlabBytes = BM * BK * 2;        // 16 KiB: one A slab
   // K blocks (64 wide) per pipeline stage. The producer/MMA handshake of a
   // stage costs about as much as six UMMA issues (measured on B200: ~360
-  // cycles per stage with no loads and no UMMAs), so the 128x64, 128x128 and
-  // 256x256 pair tiles carry two K blocks per stage: one handshake per eight
-  // UMMAs.
-  static constexpr int kKSub = ((!PAIR_ && BN_ <= 128) || (PAIR_ && SLABS_ == 1)) ? 2 : 1;
+  // cycles per stage with no loads and no UMMAs), so the smaller tiles carry
+  // several K blocks per stage: the 256x256 pair tile and the per-thread-load
+  // variants two; the TMA-fed 128 x 128 tile three and the 128 x 64 tile,
+  // whose UMMAs are the shortest (128 x 64 x 16: ~48 cycles on the tensor
+  // core, measured), four, both in two stages (1024^3 7.3 -> 6.8 us and
+  // 1024 x 1024 x 4096 20.1 -> 16.9 us on 128 x 64 tiles; 1024 x 1024 x 4096
+  // 19.8 -> 18.2 us on 128 x 128 tiles).
+  static constexpr int kKSub =
+      (!PAIR_ && BN_ == 64 && !LSU_)
+          ? 4
+          : ((!PAIR_ && BN_ == 128 && !LSU_)
+                 ? 3
+                 : (((!PAIR_ && BN_ <= 128) || (PAIR_ && SLABS_ == 1)) ? 2 : 1));
   static constexpr int kABlk = kCtaRows * BK * 2;       // A of one K block
   static constexpr int kABytes = kABlk * kKSub;
   // B boxes: N-major B as 64(N) x 64(K) boxes of 8 KiB; K-major B as one box
@@ -137,7 +146,7 @@ struct TcCfg {
   static_assert(!kPair || BN == 256, "the CTA pair runs 256-column tiles");
   static_assert(kSlabs == 1 || (kSlabs == 2 && kPair), "two slabs only for the CTA pair");
   static_assert(!kSlabN || kSlabs == 2, "N slabs come in pairs");
-  static_assert(kStages >= 3, "pipeline depth");
+  static_assert(kStages >= 2, "pipeline depth");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
   static_assert(kTmemCols <= 512, "TMEM columns");
   static_assert(kEpiChunks >= 1, "epilogue chunking");
