@@ -202,17 +202,6 @@ __global__ void __launch_bounds__(DecCfg<NM>::kThreads, 1)
         tmem_ld_cols<Cfg::kChunk>(t0 + NM + i * Cfg::kChunk, r2);
         tmem_wait_ld();
       }
-      // C of the chunk's rows, loaded before any store (a load after a store
-      // through another pointer cannot be hoisted, which would make one
-      // dependent round trip per row)
-      float prev[Cfg::kChunk];
-#pragma unroll
-      for (int j = 0; j < Cfg::kChunk; ++j) {
-        const int m = i * Cfg::kChunk + j;
-        prev[j] = (read_c && p.ksplit == 1 && m < mmax && n < p.N)
-                      ? __half2float(p.C[static_cast<size_t>(m) * p.N + n])
-                      : 0.0f;
-      }
 #pragma unroll
       for (int j = 0; j < Cfg::kChunk; ++j) {
         // an empty K range (a cluster rank past K) contributes zero
@@ -221,7 +210,9 @@ __global__ void __launch_bounds__(DecCfg<NM>::kThreads, 1)
         if (p.ksplit > 1) {
           part[m * Cfg::BMN + quad * 32 + lane] = v;
         } else if (m < mmax && n < p.N) {
-          p.C[static_cast<size_t>(m) * p.N + n] = __float2half_rn(fmaf(p.alpha, v, p.beta * prev[j]));
+          half* dst = p.C + static_cast<size_t>(m) * p.N + n;
+          const float prev = read_c ? __half2float(*dst) : 0.0f;
+          *dst = __float2half_rn(fmaf(p.alpha, v, p.beta * prev));
         }
       }
     }
