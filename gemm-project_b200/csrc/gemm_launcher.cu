@@ -654,7 +654,7 @@ void launch_pack(const PackJob& j0, const PackJob& j1, const char* name, int M, 
                  cudaStream_t s, const DeviceInfo& d) {
   const int threads = 256;
   const size_t work = static_cast<size_t>(j0.rows) * ceil_div(j0.cols, 8) +
-                      static_cast<size_t>(j1.rows) * ceil_div(j1.cols, 8);
+                      static_cast<size_t>(j1.rows) * ceil_div(j1.cols, 8);  // 16-byte chunks
   const int blocks =
       static_cast<int>(std::max<size_t>(1, std::min<size_t>((work + threads - 1) / threads,
                                                              size_t(d.sms) * 16)));

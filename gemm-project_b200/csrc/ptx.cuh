@@ -444,4 +444,50 @@ __device__ __forceinline__ unsigned short ld_stream_u16(const void* p) {
   return v;
 }
 
+// ---------------------------------------------------------------------------
+// Row segments of 64 halves at any 2-byte alignment, one thread per segment
+// (the tile kernel's per-thread operand loads and the repack kernel). The
+// thread loads the 9 aligned 16-byte lines the segment touches, only lines
+// that hold at least one element of the matrix, so nothing outside the
+// operand's 16-byte lines is read (allocations are at least 16-byte aligned).
+// It then takes the segment's 32 words from the 36 loaded words at the
+// segment's phase (its first element's position in the first line, halves
+// 0..7): two select steps move by phase / 2 words, one byte permute per word
+// moves by an odd half. Elements outside the matrix (`valid` columns of 64
+// are inside) come out as zero, as TMA's out-of-bounds fill does.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void lsu_segment_load(const uint4* line, int phase, int valid,
+                                                 uint4 (&w)[9]) {
+#pragma unroll
+  for (int i = 0; i < 9; ++i) {
+    w[i] = make_uint4(0, 0, 0, 0);
+    if (valid > 0 && 8 * i - phase < valid) w[i] = __ldg(line + i);
+  }
+}
+
+__device__ __forceinline__ void lsu_segment_shift(const uint4 (&in)[9], int phase, int valid,
+                                                  uint32_t (&out)[32]) {
+  uint32_t w[36];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) {
+    w[4 * i] = in[i].x;
+    w[4 * i + 1] = in[i].y;
+    w[4 * i + 2] = in[i].z;
+    w[4 * i + 3] = in[i].w;
+  }
+  const int q = phase >> 1;
+#pragma unroll
+  for (int i = 0; i < 34; ++i) w[i] = (q & 2) ? w[i + 2] : w[i];
+#pragma unroll
+  for (int i = 0; i < 33; ++i) w[i] = (q & 1) ? w[i + 1] : w[i];
+  const uint32_t sel = (phase & 1) ? 0x5432u : 0x3210u;
+#pragma unroll
+  for (int o = 0; o < 32; ++o) out[o] = __byte_perm(w[o], w[o + 1], sel);
+  if (valid < 64) {
+#pragma unroll
+    for (int o = 0; o < 32; ++o)
+      out[o] &= (2 * o < valid ? 0x0000FFFFu : 0u) | (2 * o + 1 < valid ? 0xFFFF0000u : 0u);
+  }
+}
+
 }  // namespace gemm_b200

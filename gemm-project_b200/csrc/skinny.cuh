@@ -291,14 +291,20 @@ struct PackJob {
   int rows, cols;
 };
 
-// Repack of up to two operands in one launch (the grid strides over the
-// 8-half groups of both). Launched as a programmatic dependent: it lets the
-// GEMM that follows start its set-up at once and waits for the kernel before
-// it (which may still write A or B) before its first load.
+// Repack of up to two operands in one launch. A thread writes one aligned
+// 16-byte chunk of the destination (8 halves; consecutive threads take
+// consecutive chunks of a row, so a warp's loads and stores are coalesced):
+// it loads the aligned 16-byte line its source chunk starts in and, when the
+// chunk is not aligned, the line after (only lines holding elements of the
+// row), and shifts by the chunk's phase. Chunks past a row's last column
+// (inside the pitch padding) are written with zeros. Launched as a
+// programmatic dependent: it lets the GEMM that follows start its set-up at
+// once and waits for the kernel before it (which may still write A or B)
+// before its first load.
 __global__ void pack_rows_kernel(const PackJob j0, const PackJob j1) {
   griddep_launch_dependents();
   griddep_wait();
-  const int g0 = (j0.cols + 7) / 8, g1 = (j1.cols + 7) / 8;
+  const int g0 = (j0.cols + 7) / 8, g1 = (j1.cols + 7) / 8;  // chunks per row
   const size_t n0 = static_cast<size_t>(j0.rows) * g0;
   const size_t total = n0 + static_cast<size_t>(j1.rows) * g1;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
@@ -309,20 +315,30 @@ __global__ void pack_rows_kernel(const PackJob j0, const PackJob j1) {
     const int groups = first ? g0 : g1;
     const int r = static_cast<int>(k / groups);
     const int c0 = static_cast<int>(k % groups) * 8;
-    const half* s = j.src + r * j.src_ld + c0;
-    half* d = j.dst + r * j.dst_ld + c0;
-    if (c0 + 8 <= j.cols) {
-      uint32_t w[4];
+    const int valid = min(8, j.cols - c0);
+    const uint64_t a = reinterpret_cast<uint64_t>(j.src + r * j.src_ld + c0);
+    const int phase = static_cast<int>((a >> 1) & 7u);
+    const uint4* line = reinterpret_cast<const uint4*>(a & ~15ull);
+    const uint4 v0 = __ldg(line);
+    uint4 v1 = make_uint4(0, 0, 0, 0);
+    if (phase + valid > 8) v1 = __ldg(line + 1);
+    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    const int q = phase >> 1;
+    uint32_t t[5];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t lo = __half_as_ushort(s[2 * q]);
-        const uint32_t hi = __half_as_ushort(s[2 * q + 1]);
-        w[q] = lo | (hi << 16);
-      }
-      *reinterpret_cast<uint4*>(d) = make_uint4(w[0], w[1], w[2], w[3]);
-    } else {
-      for (int q = 0; c0 + q < j.cols; ++q) d[q] = s[q];
+    for (int u = 0; u < 5; ++u) {
+      const uint32_t lo = (q & 1) ? w[u + 1] : w[u];
+      const uint32_t hi = (q & 1) ? w[u + 3] : w[u + 2];
+      t[u] = (q & 2) ? hi : lo;
     }
+    const uint32_t sel = (phase & 1) ? 0x5432u : 0x3210u;
+    uint32_t o[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      o[u] = __byte_perm(t[u], t[u + 1], sel);
+      if (valid < 8) o[u] &= (2 * u < valid ? 0x0000FFFFu : 0u) | (2 * u + 1 < valid ? 0xFFFF0000u : 0u);
+    }
+    *reinterpret_cast<uint4*>(j.dst + r * j.dst_ld + c0) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 

@@ -186,58 +186,6 @@ struct TcParams {
   int stall;
 };
 
-// ---------------------------------------------------------------------------
-// Per-thread operand loads (the LSU variant). A 64-half segment of one row of
-// a row-major FP16 matrix is loaded by 8 lanes, lane c taking the 16-byte chunk
-// of columns [col0 + 8c, col0 + 8c + 8). The row may start at any 2-byte
-// alignment: every lane loads the aligned 16-byte line its chunk starts in, the
-// lane of chunk 7 also the line after, and each lane takes the next line from
-// its neighbour by a shuffle, so the segment costs 8 or 9 aligned loads. Only
-// lines that hold at least one element of the matrix are loaded, so nothing
-// outside the operand's 16-byte lines is touched (allocations are at least
-// 16-byte aligned). Elements outside the matrix read as zero, as TMA's
-// out-of-bounds fill does.
-// ---------------------------------------------------------------------------
-// One 64-half row segment, owned by one thread: the 9 aligned 16-byte lines
-// it touches are loaded (only lines holding elements of the matrix), then the
-// 32 words of the segment are taken from the 36 loaded words at the
-// segment's phase (halves 0..7 into the first line): two select steps move
-// by phase / 2 words, one byte permute per word moves by an odd half.
-// Elements outside the matrix come out as zero.
-__device__ __forceinline__ void lsu_segment_load(const uint4* line, int phase, int valid,
-                                                 uint4 (&w)[9]) {
-#pragma unroll
-  for (int i = 0; i < 9; ++i) {
-    w[i] = make_uint4(0, 0, 0, 0);
-    if (valid > 0 && 8 * i - phase < valid) w[i] = __ldg(line + i);
-  }
-}
-
-__device__ __forceinline__ void lsu_segment_shift(const uint4 (&in)[9], int phase, int valid,
-                                                  uint32_t (&out)[32]) {
-  uint32_t w[36];
-#pragma unroll
-  for (int i = 0; i < 9; ++i) {
-    w[4 * i] = in[i].x;
-    w[4 * i + 1] = in[i].y;
-    w[4 * i + 2] = in[i].z;
-    w[4 * i + 3] = in[i].w;
-  }
-  const int q = phase >> 1;
-#pragma unroll
-  for (int i = 0; i < 34; ++i) w[i] = (q & 2) ? w[i + 2] : w[i];
-#pragma unroll
-  for (int i = 0; i < 33; ++i) w[i] = (q & 1) ? w[i + 1] : w[i];
-  const uint32_t sel = (phase & 1) ? 0x5432u : 0x3210u;
-#pragma unroll
-  for (int o = 0; o < 32; ++o) out[o] = __byte_perm(w[o], w[o + 1], sel);
-  if (valid < 64) {
-#pragma unroll
-    for (int o = 0; o < 32; ++o)
-      out[o] &= (2 * o < valid ? 0x0000FFFFu : 0u) | (2 * o + 1 < valid ? 0xFFFF0000u : 0u);
-  }
-}
-
 // Grouped raster over output tiles so that concurrently resident CTAs share A
 // and B panels in L2. group > 0: `group` tile-rows advance together along N;
 // group < 0: |group| tile-columns advance together along M.
