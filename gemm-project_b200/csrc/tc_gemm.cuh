@@ -52,9 +52,18 @@
 //                 registers while the UMMAs run, and between reading slab 0 and
 //                 slab 1 out of TMEM there is only register arithmetic, so the
 //                 next tile starts about a microsecond after this one ends.
+// LSU variant (template flag; the 128 x 64 and 128 x 128 tiles): A and B at
+// any 2-byte alignment and row pitch are read in place. Warp 0 issues no TMA;
+// before each tile's epilogue the eight epilogue warps load its K blocks with
+// per-thread loads, one 64-half row segment per thread per K block, and write
+// them into the same 128B-swizzled stages (fence.proxy.async, then one
+// arrival per warp on the stage's `full` barrier).
 // No TMA load uses cluster multicast, and no operand is another GPU's memory.
 // Every mbarrier wait is bounded (ptx.cuh mbar_wait): on expiry the kernel
-// records an error code and unwinds; it never traps.
+// records an error code and unwinds (the epilogue first waits, bounded, for C
+// boxes it already requested; a split-K cluster with an aborted CTA writes no
+// C); it never traps. TcParams::stall (the self test gemm_selftest_stall) turns
+// the operand feed off so that these waits run out on purpose.
 #pragma once
 
 #include "ptx.cuh"
