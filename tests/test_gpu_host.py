@@ -2,7 +2,8 @@
 
 CPU tests: argument checks (no device work). GPU tests: parity with the CPU
 oracle on the same seeded inputs, for one and several slabs, ragged slab
-counts, beta == 0 (C not sent) and beta != 0, out != c.
+counts, beta == 0 (C not sent) and beta != 0, out != c, and B already on the
+device.
 """
 import pytest
 import torch
@@ -50,4 +51,22 @@ def test_in_place_and_repeated(lib, cuda):
     torch.cuda.current_stream().synchronize()
     once = oracle.reference_fp32(a, b, c, 1.0, 1.0).half()
     chk = oracle.check(c_h, oracle.reference_fp32(a, b, once, 1.0, 1.0))
+    assert chk.passed, str(chk)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("beta", [0.0, -0.25])
+def test_device_resident_b(lib, cuda, beta):
+    """B already on the device (a resident weight, or a replica a multi-GPU job
+    broadcast once): only A (and C when beta != 0) cross PCIe; B is not modified."""
+    m, n, k = 1500, 1032, 776
+    a, b, c = oracle.make_inputs(m, n, k, "normal", 11)
+    b_d = b.to(cuda)
+    a_h, c_h = a.pin_memory(), c.pin_memory()
+    out = torch.empty_like(c_h).pin_memory()
+    gemm_b200.gemm_host(a_h, b_d, c_h, 0.75, beta, out=out, slabs=4)
+    torch.cuda.current_stream().synchronize()
+    assert lib.gemm_launcher_status() == 0
+    assert torch.equal(b_d.cpu(), b)
+    chk = oracle.check(out, oracle.reference_fp32(a, b, c, 0.75, beta))
     assert chk.passed, str(chk)
