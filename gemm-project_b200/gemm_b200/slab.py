@@ -162,6 +162,32 @@ class SlabGemm:
         opts.is_high_priority_stream = True
         return dist.new_group(ranks=ranks, backend="nccl", pg_options=opts)
 
+    # Rates for broadcast_and_run's SM reservation model (measured on B200s: NCCL
+    # broadcast over NVLink 580-680 GB/s, the slab GEMM 1.2-1.5 PFLOP/s), and the
+    # margin on the broadcast's modelled end. A block that takes every SM while
+    # a broadcast kernel is still queued stalls the broadcast for a whole block
+    # GEMM, while reserving SMs one block too long costs about a tenth of one,
+    # so the margin errs on the long side.
+    BCAST_BYTES_PER_S = 6.0e11
+    GEMM_FLOP_PER_S = 1.3e15
+    BCAST_MARGIN = 1.5
+
+    @classmethod
+    def reserve_schedule(cls, rows: int, k: int, widths: list[int], elem_bytes: int = 2) -> list[bool]:
+        """For each column block of broadcast_and_run, whether its GEMM leaves
+        SMs free for the broadcast: True while the block's modelled start
+        (one block's broadcast plus the earlier blocks' GEMMs) falls before
+        BCAST_MARGIN times the modelled end of the whole broadcast. The last
+        block never reserves (nothing is left to broadcast after it lands)."""
+        total = sum(widths)
+        t_end = cls.BCAST_MARGIN * k * total * elem_bytes / cls.BCAST_BYTES_PER_S
+        start = k * widths[0] * elem_bytes / cls.BCAST_BYTES_PER_S if widths else 0.0
+        out = []
+        for j, w in enumerate(widths):
+            out.append(j + 1 < len(widths) and start < t_end)
+            start += 2.0 * rows * w * k / cls.GEMM_FLOP_PER_S
+        return out
+
     def broadcast_and_run(self, a_slab: torch.Tensor, b: torch.Tensor, c_slab: torch.Tensor,
                           alpha: float = 1.0, beta: float = 0.0, src: int = 0, chunks: int = 8,
                           reserve_sms: int = 16,
@@ -173,9 +199,12 @@ class SlabGemm:
         last block takes the rest). On `src` each block is packed,
         and all blocks are broadcast asynchronously in order. Each rank's stream
         waits for block j, then computes C[:, block j] = alpha * A @ B[:, block j]
-        + beta * C[:, block j] while blocks j+1.. are in flight. Until the last
-        block, the GEMM leaves `reserve_sms` SMs free, because the collective's
-        kernels cannot start while a persistent GEMM holds every SM. Returns the
+        + beta * C[:, block j] while blocks j+1.. are in flight. While blocks are
+        still in flight the GEMM leaves `reserve_sms` SMs free, because the
+        collective's kernels cannot start while a persistent GEMM holds every
+        SM; the blocks computed after the broadcast has ended take every SM.
+        Which blocks those are comes from reserve_schedule's model of the two
+        rates. Returns the
         blocks, which hold this rank's replica of B in column-block layout.
         Ranks must call it collectively with the same chunks. With
         `deadline_s`, the host then waits at most that long for every block
@@ -197,9 +226,10 @@ class SlabGemm:
             blocks.append(blk)
         total_sms = (torch.cuda.get_device_properties(b.device).multi_processor_count
                      if b.is_cuda else 0)
-        for j, ((c0, c1), blk, work) in enumerate(zip(bounds, blocks, works)):
+        reserve = self.reserve_schedule(a_slab.shape[0], k, [c1 - c0 for c0, c1 in bounds],
+                                        b.element_size())
+        for (c0, c1), blk, work, pending in zip(bounds, blocks, works, reserve):
             work.wait()  # this stream waits for block j; the host does not block
-            pending = j + 1 < len(bounds)
             max_sms = max(2, total_sms - reserve_sms) if (pending and total_sms) else 0
             if a_slab.shape[0]:
                 self.compute_sub(a_slab, blk, c_slab[:, c0:c1], alpha, beta, max_sms)

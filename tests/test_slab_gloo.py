@@ -158,3 +158,21 @@ def test_stalled_rank_hits_host_deadline():
     assert by_rank[0][1] == "collective_error", results
     assert by_rank[0][3] == "CommDeadlineExceeded", results
     assert by_rank[0][2] < 4.0, results
+
+
+def test_reserve_schedule():
+    """broadcast_and_run leaves SMs free only for blocks whose GEMM starts
+    before the broadcast's modelled end (with its margin), never for the last."""
+    sys.path.insert(0, str(REPO / "gemm-project_b200"))
+    from gemm_b200.slab import SlabGemm
+
+    k, widths = 16384, [4096] * 8
+    # 4096-row slab: one block's GEMM (0.42 ms) is about twice one block's
+    # broadcast (0.22 ms); the broadcast's end (1.8 ms, x1.5) falls in block 5
+    assert SlabGemm.reserve_schedule(4096, k, widths) == [True] * 6 + [False] * 2
+    # 8192-row slab: blocks 0-2 start before it
+    assert SlabGemm.reserve_schedule(8192, k, widths) == [True] * 3 + [False] * 5
+    # a slab so small that every GEMM finishes before the next block lands
+    assert SlabGemm.reserve_schedule(16, k, widths) == [True] * 7 + [False]
+    assert SlabGemm.reserve_schedule(4096, k, [8]) == [False]
+    assert SlabGemm.reserve_schedule(4096, k, []) == []
