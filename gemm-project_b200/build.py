@@ -30,6 +30,7 @@ EXPORTS = [
     "gemm_last_kernel", "gemm_cublas", "gemm_cublas_stream", "gemm_slab_rows",
     "gemm_selftest_wait_timeout", "gemm_launcher_noalloc", "gemm_launcher_tn",
     "launchGemmSample", "gemm_launch_error", "gemm_launcher_sub", "gemm_selftest_stall",
+    "gemm_peer_export", "gemm_peer_open", "gemm_peer_close", "gemm_peer_copy2d", "gemm_peer_flags",
 ]
 
 

@@ -37,6 +37,7 @@
 #include "stream.cuh"
 #include "decode.cuh"
 #include "tc_gemm.cuh"
+#include "peer.cuh"
 
 namespace gemm_b200 {
 
@@ -323,6 +324,21 @@ EncodeTiledFn encode_fn() {
         q != cudaDriverEntryPointSuccess)
       return static_cast<EncodeTiledFn>(nullptr);
     return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+using MemGetAddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+MemGetAddressRangeFn address_range_fn() {
+  static MemGetAddressRangeFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<MemGetAddressRangeFn>(nullptr);
+    return reinterpret_cast<MemGetAddressRangeFn>(p);
   }();
   return fn;
 }
@@ -1408,4 +1424,81 @@ extern "C" GEMM_API int gemm_selftest_wait_timeout(int timeout_us, cudaStream_t 
   record_error(cudaGetLastError());
   record_error(cudaStreamSynchronize(stream));
   return gemm_launcher_status();
+}
+
+// ---------------------------------------------------------------------------
+// Peer memory and the copy-engine ring (multi-GPU replication of B).
+// ---------------------------------------------------------------------------
+extern "C" GEMM_API int gemm_peer_export(const void* ptr, void* handle, unsigned long long* offset) {
+  if (ptr == nullptr || handle == nullptr || offset == nullptr) return -1;
+  MemGetAddressRangeFn range = address_range_fn();
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range == nullptr || range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return -1;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) {
+    record_error(e);
+    return -1;
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base);
+  return 0;
+}
+
+extern "C" GEMM_API int gemm_peer_open(const void* handle, void** base) {
+  if (handle == nullptr || base == nullptr) return -1;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    record_error(e);
+    return -1;
+  }
+  return 0;
+}
+
+extern "C" GEMM_API int gemm_peer_close(void* base) {
+  if (base == nullptr) return -1;
+  const cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) {
+    record_error(e);
+    return -1;
+  }
+  return 0;
+}
+
+extern "C" GEMM_API int gemm_peer_copy2d(void* dst, size_t dst_pitch, const void* src,
+                                         size_t src_pitch, size_t width_bytes, size_t rows,
+                                         cudaStream_t stream) {
+  if (rows == 0 || width_bytes == 0) return 0;
+  if (dst == nullptr || src == nullptr || dst_pitch < width_bytes || src_pitch < width_bytes)
+    return -1;
+  const cudaError_t e = cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, width_bytes, rows,
+                                          cudaMemcpyDeviceToDevice, stream);
+  if (e != cudaSuccess) {
+    record_error(e);
+    return -1;
+  }
+  return 0;
+}
+
+extern "C" GEMM_API int gemm_peer_flags(int* signal0, int value0, int* signal1, int value1,
+                                        const int* wait0, int wait_value0, const int* wait1,
+                                        int wait_value1, long long timeout_us,
+                                        cudaStream_t stream) {
+  DeviceInfo& d = device_info();
+  const PeerFlagStep step{{signal0, signal1}, {value0, value1}, {wait0, wait1},
+                          {wait_value0, wait_value1}};
+  const unsigned long long timeout_ns =
+      timeout_us > 0 ? static_cast<unsigned long long>(timeout_us) * 1000ull : wait_timeout_ns();
+  log_launch("peer_flag_kernel", 0, 0, 0, dim3(1), dim3(32));
+  peer_flag_kernel<<<1, 32, 0, stream>>>(step, timeout_ns, d.err);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    record_error(e);
+    return -1;
+  }
+  return 0;
 }

@@ -25,6 +25,7 @@ enum DeviceError : int {
   kErrTimeoutEpilogue = 3,    // epilogue waited too long for a finished accumulator
   kErrTimeoutCluster = 4,     // cluster barrier in the skinny kernel
   kErrTimeoutProbe = 5,       // the wait-probe test kernel (expected by its test)
+  kErrTimeoutPeer = 6,        // a peer GPU's flag in the B replication ring never came
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {

@@ -58,6 +58,17 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gemm_launcher_sub.restype = i
     lib.gemm_selftest_stall.argtypes = [vp, vp, vp, i, i, i, i, i, i, vp]
     lib.gemm_selftest_stall.restype = i
+    sz = ctypes.c_size_t
+    lib.gemm_peer_export.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_ulonglong)]
+    lib.gemm_peer_export.restype = i
+    lib.gemm_peer_open.argtypes = [vp, ctypes.POINTER(vp)]
+    lib.gemm_peer_open.restype = i
+    lib.gemm_peer_close.argtypes = [vp]
+    lib.gemm_peer_close.restype = i
+    lib.gemm_peer_copy2d.argtypes = [vp, sz, vp, sz, sz, sz, vp]
+    lib.gemm_peer_copy2d.restype = i
+    lib.gemm_peer_flags.argtypes = [vp, i, vp, i, vp, i, vp, i, ctypes.c_longlong, vp]
+    lib.gemm_peer_flags.restype = i
     return lib
 
 

@@ -15,6 +15,13 @@ has landed, while the next blocks are still in flight. Every output element
 still takes its whole K range in one kernel, so the arithmetic is that of the
 plain path. Splitting along K would instead round C to FP16 between blocks.
 
+`PeerRing` does the same without NCCL: B's column chunks travel along a ring of
+the ranks by copy-engine copies from the predecessor's IPC-mapped replica, so
+the slab GEMM keeps every SM but one pair, where NCCL's kernels needed 16. The
+ranks order the copies through flag words in each other's memory, set and
+awaited by a one-thread kernel with a bounded wait (`ring_program` states the
+protocol; the library's gemm_peer_* entry points carry it out).
+
 One process per GPU; the group comes from `torch.distributed`. The compute steps
 are injectable so the host logic (partition, broadcast, gather) is testable on
 CPU ranks with the gloo backend.
@@ -30,6 +37,7 @@ communicators, whose calls never hold the host.
 """
 from __future__ import annotations
 
+import ctypes
 import time
 from typing import Callable, Optional
 
@@ -256,3 +264,267 @@ class SlabGemm:
             return None
         rows = [slab_rows(m, self.world, r)[1] for r in range(self.world)]
         return torch.cat([p[:r] for p, r in zip(parts, rows)], dim=0)
+
+
+# ---------------------------------------------------------------------------
+# Copy-engine ring (PeerRing)
+# ---------------------------------------------------------------------------
+def ring_layout(n: int, chunk_cols: int = 2048, block_cols: int = 4096, first_chunk_cols: int = 512,
+                first_block_cols: int = 2048) -> tuple[list, list]:
+    """Column chunks and GEMM blocks of PeerRing over N = n columns, as
+    ([(c0, c1) per chunk], [end chunk index per block]).
+
+    Chunk widths start at first_chunk_cols and double up to chunk_cols, so that
+    the first columns cross the ring's hops quickly; the last chunk takes the
+    rest. A GEMM block is a run of whole chunks: the first one ends at the first
+    chunk boundary at or past first_block_cols, each later one at the first
+    boundary at least block_cols further on; a remainder narrower than half a
+    block joins the last full block. All widths are multiples of 8 columns."""
+    for v in (chunk_cols, block_cols, first_chunk_cols, first_block_cols):
+        if v < 8 or v % 8:
+            raise ValueError("chunk and block widths must be positive multiples of 8")
+    bounds, c0, w = [], 0, min(first_chunk_cols, chunk_cols)
+    while c0 < n:
+        bounds.append((c0, min(n, c0 + w)))
+        c0 += w
+        w = min(2 * w, chunk_cols)
+    block_ends, target = [], first_block_cols
+    for j, (_, c1) in enumerate(bounds):
+        # a remainder under half a block joins this block instead of running alone
+        if j == len(bounds) - 1 or (c1 >= target and n - c1 >= block_cols // 2):
+            block_ends.append(j + 1)
+            target = c1 + block_cols
+    return bounds, block_ends
+
+
+def ring_program(position: int, world: int, n_chunks: int, block_ends: list[int],
+                 seq: int) -> tuple[list, list]:
+    """The operations one rank issues in call `seq` (1, 2, ...) of PeerRing, as
+    (copy_stream_ops, compute_stream_ops). `position` is the rank's place on the
+    ring (0 = the source, which holds B; position p copies from p - 1). GEMM
+    block g covers chunks [block_ends[g - 1], block_ends[g]).
+
+    Each rank owns two flag words, both monotone counters over the calls:
+    `ready`, set by its predecessor to the number of chunks it may copy so far,
+    and `consumed`, set by its successor to the number of chunks the successor
+    has copied. With n = n_chunks and base = (seq - 1) * n:
+
+    copy stream (positions >= 1):
+      ("join_compute",)           wait for this rank's earlier compute-stream work
+                                  (the previous call's GEMMs read the replica)
+      for chunk j:
+        ("flags", signals, waits) signal ready_succ = base + j (chunk j - 1 is
+                                  here), then wait until ready >= base + j + 1
+        ("copy", j)               chunk j from the predecessor's replica
+        ("block_ready", g)        after the last chunk of GEMM block g
+      ("flags", signals, [])      ready_succ = consumed_pred = base + n
+      ("block_ready", last)       the last block's only after that final signal,
+                                  since its GEMM leaves no SM free
+    compute stream:
+      position 0 first signals ready_succ = base + n: all of B is there;
+      ("gemm", g, reserve)        block g, after its block_ready on positions
+                                  >= 1; `reserve` asks the GEMM to leave SMs
+                                  free for the copy stream's flag kernels
+      a rank with a successor ends with a wait until consumed >= base + n, so
+      that neither the caller (on position 0) nor the next call overwrites
+      chunks the successor is still copying.
+
+    A signal is ("succ" | "pred", "ready" | "consumed", value); a wait is
+    ("ready" | "consumed", value), satisfied once the word minus the value is
+    >= 0."""
+    if not (0 <= position < world and n_chunks >= 1 and seq >= 1 and block_ends
+            and block_ends[-1] == n_chunks
+            and all(a < b for a, b in zip([0] + block_ends, block_ends))):
+        raise ValueError("bad ring program arguments")
+    n_blocks = len(block_ends)
+    ends = set(block_ends[:-1])
+    base = (seq - 1) * n_chunks
+    has_succ = position + 1 < world
+    copy_ops, compute_ops = [], []
+    if position == 0:
+        if has_succ:
+            compute_ops.append(("flags", [("succ", "ready", base + n_chunks)], []))
+        compute_ops += [("gemm", g, False) for g in range(n_blocks)]
+    else:
+        copy_ops.append(("join_compute",))
+        for j in range(n_chunks):
+            signals = [("succ", "ready", base + j)] if (has_succ and j > 0) else []
+            copy_ops.append(("flags", signals, [("ready", base + j + 1)]))
+            copy_ops.append(("copy", j))
+            if j + 1 in ends:
+                copy_ops.append(("block_ready", block_ends.index(j + 1)))
+        final = [("succ", "ready", base + n_chunks)] if has_succ else []
+        copy_ops.append(("flags", final + [("pred", "consumed", base + n_chunks)], []))
+        # the last block's GEMM takes every SM, so it starts only after the
+        # final signal has gone out
+        copy_ops.append(("block_ready", n_blocks - 1))
+        compute_ops += [("gemm", g, g + 1 < n_blocks) for g in range(n_blocks)]
+    if has_succ:
+        compute_ops.append(("flags", [], [("consumed", base + n_chunks)]))
+    return copy_ops, compute_ops
+
+
+class PeerRing:
+    """B replicated from `src` to every rank of `group` by copy engines along a
+    ring, and the row-slab GEMM run block by block as B's column chunks land.
+
+    `b` is this rank's [K, N] FP16 replica buffer, contiguous, on this rank's
+    GPU. On `src` it holds B (the caller writes it, in stream order, before each
+    call); elsewhere every call overwrites it with B, so it doubles as the
+    resident replica afterwards. Construction is collective: the ranks exchange
+    IPC handles of their replicas and flag words and map their ring neighbours'.
+    Every rank must be on its own GPU (checked): the flag kernels of two ranks
+    that wait on each other must never share one.
+
+    Chunks and GEMM blocks follow ring_layout (chunk widths growing from
+    first_chunk_cols to chunk_cols; blocks of first_block_cols, then block_cols).
+    Chunks move by cudaMemcpy2DAsync on a high-priority stream. Every output
+    element takes its whole K range in one kernel, so C is bit-identical to the
+    plain path."""
+
+    def __init__(self, b: torch.Tensor, group: Optional[dist.ProcessGroup] = None, src: int = 0,
+                 chunk_cols: int = 2048, block_cols: int = 4096, first_chunk_cols: int = 512,
+                 first_block_cols: int = 2048, reserve_sms: int = 2, timeout_s: float = 10.0,
+                 compute_sub: Optional[Callable] = None):
+        if b.dtype != torch.float16 or not b.is_cuda or b.dim() != 2 or not b.is_contiguous():
+            raise ValueError("b must be a contiguous 2-D CUDA float16 tensor")
+        from . import load
+        self.lib = load()
+        self.group, self.b = group, b
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.src = src
+        self.k, self.n = b.shape
+        self.bounds, self.block_ends = ring_layout(self.n, chunk_cols, block_cols, first_chunk_cols,
+                                                   first_block_cols)
+        self.blocks = [(self.bounds[j0][0], self.bounds[j1 - 1][1])
+                       for j0, j1 in zip([0] + self.block_ends[:-1], self.block_ends)]
+        self.reserve_sms = reserve_sms
+        self.timeout_us = int(timeout_s * 1e6)
+        self.compute_sub = compute_sub or _gpu_compute_sub
+        self.position = (self.rank - src) % self.world
+        self.seq = 0
+        self.flags = torch.zeros(2, dtype=torch.int32, device=b.device)  # [ready, consumed]
+        self.copy_stream = torch.cuda.Stream(device=b.device, priority=-1)
+        self.events = [torch.cuda.Event() for _ in self.blocks]
+        self.total_sms = torch.cuda.get_device_properties(b.device).multi_processor_count
+        self._mapped: dict[bytes, int] = {}
+        torch.cuda.synchronize(b.device)
+
+        mine = {"b": self._export(b), "flags": self._export(self.flags),
+                "uuid": str(torch.cuda.get_device_properties(b.device).uuid),
+                "shape": (self.k, self.n, tuple(self.bounds), tuple(self.block_ends), src)}
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=group)
+        if len({e["uuid"] for e in everyone}) != self.world:
+            raise RuntimeError("PeerRing needs one GPU per rank; two ranks share a GPU")
+        if len({e["shape"] for e in everyone}) != 1:
+            raise ValueError("ranks disagree on B's shape or the ring's chunking")
+        ring = [(src + p) % self.world for p in range(self.world)]
+        self.pred = ring[self.position - 1] if self.position > 0 else None
+        self.succ = ring[self.position + 1] if self.position + 1 < self.world else None
+        self.pred_b = self.pred_flags = self.succ_flags = None
+        if self.pred is not None:
+            self.pred_b = self._open(everyone[self.pred]["b"])
+            self.pred_flags = self._open(everyone[self.pred]["flags"])
+        if self.succ is not None:
+            self.succ_flags = self._open(everyone[self.succ]["flags"])
+        self.closed = False
+        dist.barrier(group=group)
+
+    def _export(self, t: torch.Tensor) -> tuple[bytes, int]:
+        handle = ctypes.create_string_buffer(64)
+        offset = ctypes.c_ulonglong()
+        if self.lib.gemm_peer_export(t.data_ptr(), handle, ctypes.byref(offset)) != 0:
+            raise RuntimeError(f"gemm_peer_export failed (CUDA error {self.lib.gemm_launch_error()})")
+        return handle.raw, offset.value
+
+    def _open(self, exported: tuple[bytes, int]) -> int:
+        handle, offset = exported
+        if handle not in self._mapped:
+            base = ctypes.c_void_p()
+            if self.lib.gemm_peer_open(handle, ctypes.byref(base)) != 0:
+                raise RuntimeError(f"gemm_peer_open failed (CUDA error {self.lib.gemm_launch_error()})")
+            self._mapped[handle] = base.value
+        return self._mapped[handle] + offset
+
+    def close(self) -> None:
+        """Unmap the neighbours' memory (collective: after every rank's last
+        call has completed on the device)."""
+        torch.cuda.synchronize(self.b.device)
+        dist.barrier(group=self.group)
+        for base in self._mapped.values():
+            self.lib.gemm_peer_close(base)
+        self._mapped.clear()
+        self.pred_b = self.pred_flags = self.succ_flags = None
+        self.closed = True
+
+    def _flags(self, signals, waits, stream) -> None:
+        sig = [(None, 0), (None, 0)]
+        for i, (who, which, value) in enumerate(signals):
+            base = self.succ_flags if who == "succ" else self.pred_flags
+            sig[i] = (base + (0 if which == "ready" else 4), value)
+        wt = [(None, 0), (None, 0)]
+        for i, (which, value) in enumerate(waits):
+            wt[i] = (self.flags.data_ptr() + (0 if which == "ready" else 4), value)
+        if self.lib.gemm_peer_flags(sig[0][0], sig[0][1], sig[1][0], sig[1][1], wt[0][0], wt[0][1],
+                                    wt[1][0], wt[1][1], self.timeout_us, stream.cuda_stream) != 0:
+            raise RuntimeError("gemm_peer_flags launch failed")
+
+    def broadcast_and_run(self, a_slab: torch.Tensor, c_slab: torch.Tensor, alpha: float = 1.0,
+                          beta: float = 0.0, deadline_s: Optional[float] = None) -> torch.Tensor:
+        """One call (collective, every rank in the same order): B from `src`
+        into every rank's replica, and this rank's C slab = alpha * A_slab @ B +
+        beta * C_slab, block by block as B's chunks land. Asynchronous on the
+        current stream; returns the replica. With `deadline_s`, the host waits
+        for the call to finish on the device for at most that long and raises
+        CommDeadlineExceeded if it did not, or if a flag wait ran out (library
+        status 1006)."""
+        if self.closed:
+            raise RuntimeError("PeerRing is closed")
+        self.seq += 1
+        compute = torch.cuda.current_stream(self.b.device)
+        copy_ops, compute_ops = ring_program(self.position, self.world, len(self.bounds),
+                                             self.block_ends, self.seq)
+        esz = self.b.element_size()
+        row_bytes = self.n * esz
+        for op in copy_ops:
+            if op[0] == "join_compute":
+                self.copy_stream.wait_stream(compute)
+            elif op[0] == "flags":
+                self._flags(op[1], op[2], self.copy_stream)
+            elif op[0] == "copy":
+                c0, c1 = self.bounds[op[1]]
+                if self.lib.gemm_peer_copy2d(self.b.data_ptr() + c0 * esz, row_bytes,
+                                             self.pred_b + c0 * esz, row_bytes, (c1 - c0) * esz,
+                                             self.k, self.copy_stream.cuda_stream) != 0:
+                    raise RuntimeError("gemm_peer_copy2d failed")
+            elif op[0] == "block_ready":
+                self.events[op[1]].record(self.copy_stream)
+        for op in compute_ops:
+            if op[0] == "flags":
+                self._flags(op[1], op[2], compute)
+            elif op[0] == "gemm":
+                g, reserve = op[1], op[2]
+                if self.position > 0:
+                    compute.wait_event(self.events[g])
+                c0, c1 = self.blocks[g]
+                max_sms = max(2, self.total_sms - self.reserve_sms) if reserve else 0
+                if a_slab.shape[0]:
+                    self.compute_sub(a_slab, self.b[:, c0:c1], c_slab[:, c0:c1], alpha, beta, max_sms)
+        if deadline_s is not None:
+            done = torch.cuda.Event()
+            done.record(compute)
+            t0 = time.monotonic()
+            while not done.query():
+                if time.monotonic() - t0 > deadline_s:
+                    raise CommDeadlineExceeded(
+                        f"ring broadcast of B: not complete after {deadline_s:.3g} s")
+                time.sleep(0.0005)
+            from . import status
+            st = status()
+            if st == 1006:
+                raise CommDeadlineExceeded("ring broadcast of B: a peer flag wait ran out")
+            if st != 0:
+                raise RuntimeError(f"ring broadcast of B: library status {st}")
+        return self.b

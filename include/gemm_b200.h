@@ -152,7 +152,8 @@ GEMM_API int gemm_launcher_noalloc(const gemm_half_t* A, const gemm_half_t* B, g
  * every call since the last query launched and no kernel reported an error,
  * a cudaError_t value (1..999) for the first failed launch on this thread, or
  * 1000 + code for a device-side bounded wait that ran out
- * (1001 operand producer or loader, 1002 MMA issuer, 1003 epilogue, 1005 wait probe).
+ * (1001 operand producer or loader, 1002 MMA issuer, 1003 epilogue, 1005 wait probe,
+ * 1006 peer flag of the B replication ring).
  * Reading the device word synchronizes with the legacy default stream.
  * The status is cleared by the call. */
 GEMM_API int gemm_launcher_status(void);
@@ -176,6 +177,39 @@ GEMM_API void gemm_cublas_stream(const gemm_half_t* A, const gemm_half_t* B, gem
  * [*row0, *row0 + return value); the first M % world ranks get one extra row.
  * Returns -1 on invalid arguments. Pure host function. */
 GEMM_API int gemm_slab_rows(int M, int world, int rank, int* row0);
+
+/* Peer memory and the copy-engine ring that replicates B over the ranks of a
+ * multi-GPU row-slab job (no counterpart in the reference, which is
+ * single-GPU; used by gemm_b200.slab.PeerRing). One process per GPU.
+ *
+ * gemm_peer_export: the 64-byte IPC handle (cudaIpcGetMemHandle) of the device
+ * allocation that holds `ptr`, and the offset of `ptr` in it.
+ * gemm_peer_open: maps another process's exported allocation into the current
+ * device (cudaIpcOpenMemHandle, peer access enabled on demand) and returns its
+ * base; add the exporter's offset. gemm_peer_close unmaps it.
+ * Each returns 0, or -1 (the CUDA error goes to gemm_launch_error()). */
+GEMM_API int gemm_peer_export(const void* ptr, void* handle, unsigned long long* offset);
+GEMM_API int gemm_peer_open(const void* handle, void** base);
+GEMM_API int gemm_peer_close(void* base);
+
+/* Stream-ordered copy-engine copy of `rows` rows of `width_bytes` bytes
+ * (cudaMemcpy2DAsync); either side may be peer memory mapped by
+ * gemm_peer_open. Uses no SM. Returns 0 or -1. */
+GEMM_API int gemm_peer_copy2d(void* dst, size_t dst_pitch, const void* src, size_t src_pitch,
+                              size_t width_bytes, size_t rows, cudaStream_t stream);
+
+/* One-thread flag step on `stream`: sets *signal0 = value0 and
+ * *signal1 = value1 (system-scope release stores; null pointers are skipped),
+ * then waits until *wait0 - wait_value0 >= 0 and *wait1 - wait_value1 >= 0
+ * (system-scope acquire loads, wrap-safe signed differences; null pointers are
+ * skipped) for at most timeout_us microseconds (<= 0: GEMM_WAIT_TIMEOUT_MS).
+ * A wait that runs out records code 6 in the device error word, which
+ * gemm_launcher_status() then returns as 1006, and the kernel returns; once the
+ * word is set, later flag steps skip their waits. Returns 0 or -1 (launch
+ * error). */
+GEMM_API int gemm_peer_flags(int* signal0, int value0, int* signal1, int value1, const int* wait0,
+                             int wait_value0, const int* wait1, int wait_value1,
+                             long long timeout_us, cudaStream_t stream);
 
 /* Failure-detection self test (no counterpart in the reference): launches a
  * one-CTA kernel that waits on an mbarrier nothing will complete, bounded by

@@ -1,8 +1,10 @@
 """One rank of tests/test_multigpu_nccl.py (launched by torchrun, one process per GPU).
 
 Runs the multi-GPU row-slab launcher on real GPUs over NCCL and checks it against
-the CPU oracle: SlabGemm.broadcast_b + run, and the overlapped
-broadcast_and_run (B in column blocks), each on a ragged shape (M not a
+the CPU oracle: SlabGemm.broadcast_b + run, the overlapped
+broadcast_and_run (B in column blocks), and PeerRing (B along a ring of
+copy-engine copies, three calls in a row with B rewritten on the source before
+the last), each on a ragged shape (M not a
 multiple of the rank count or of the tile heights, N and K not multiples of
 the tile widths), with beta != 0 and with beta == 0 over a NaN-filled C. The
 slabs are gathered with gather_c and rank 0 compares the whole C with the
@@ -23,7 +25,7 @@ def main():
     import torch
     import torch.distributed as dist
     import gemm_b200
-    from gemm_b200.slab import SlabGemm
+    from gemm_b200.slab import PeerRing, SlabGemm
     from oracle import oracle
 
     rank = int(os.environ["RANK"])
@@ -80,10 +82,45 @@ def main():
             st = gemm_b200.status()
             if st != 0:
                 failures.append(f"library status {st}")
+        # copy-engine ring: three calls in a row on one PeerRing, B rewritten on
+        # the source before the third; 9 chunks (8 of 256 columns and one of 8)
+        # in GEMM blocks of 3 chunks
+        b_alt = oracle.make_inputs(m, n, k, "normal", seed=43)[1]
+        row0, rows = SlabGemm().partition(m)
+        a_slab = a[row0:row0 + rows].to(dev)
+        b_ring = b_full.to(dev) if rank == 0 else torch.full((k, n), float("nan"), device=dev,
+                                                             dtype=torch.float16)
+        ring = PeerRing(b_ring, chunk_cols=256, block_cols=768, first_chunk_cols=256,
+                        first_block_cols=768, timeout_s=20.0)
+        if ring.blocks != [(0, 768), (768, 1536), (1536, 2056)]:
+            failures.append(f"ring blocks {ring.blocks}")
+        for call, (alpha, beta, b_src) in enumerate(((0.75, -0.25, b_full), (1.0, 0.0, b_full),
+                                                     (0.5, 0.25, b_alt))):
+            if rank == 0 and call == 2:
+                b_ring.copy_(b_alt.to(dev))
+            c_init = c0[row0:row0 + rows] if beta != 0 else torch.full((rows, n), float("nan"),
+                                                                       dtype=torch.float16)
+            c3 = c_init.to(dev)
+            ring.broadcast_and_run(a_slab, c3, alpha, beta, deadline_s=30.0)
+            if not torch.equal(b_ring.cpu(), b_src):
+                failures.append(f"ring call {call}: replica of B differs")
+            full3 = SlabGemm().gather_c(c3, m)
+            if rank == 0:
+                chk = oracle.check(full3, oracle.reference_fp32(a, b_src, c0, alpha, beta))
+                if not chk.passed:
+                    failures.append(f"ring call {call} beta={beta}: {chk}")
+        ring.close()
+        st = gemm_b200.status()
+        if st != 0:
+            failures.append(f"library status {st} after the ring")
         dist.barrier()
     except Exception:
         failures.append(traceback.format_exc().replace("\n", " | "))
-    print(f"RESULT {rank} {'ok' if not failures else '; '.join(failures)}", flush=True)
+    # one write() per line: the ranks share the pipe, and a single write of up to
+    # PIPE_BUF bytes is never interleaved with another process's
+    line = f"RESULT {rank} {'ok' if not failures else '; '.join(failures)}"[:3000] + "\n"
+    sys.stdout.flush()
+    os.write(1, line.encode())
     dist.destroy_process_group()
 
 

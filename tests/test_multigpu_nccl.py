@@ -1,4 +1,5 @@
-"""The multi-GPU row-slab launcher on two real GPUs over NCCL (needs >= 2 B200s).
+"""The multi-GPU row-slab launcher on real GPUs, over NCCL and over the
+copy-engine ring (needs >= 2 B200s; uses up to 4).
 
 Marked `multigpu`, not `gpu`: the single-GPU suite (`-m gpu`) runs on one B200,
 so this test runs on its own on a two-GPU box
@@ -9,6 +10,7 @@ group timeout and an outer `timeout` as the last bound) and requires every rank
 to report that its results and its replica of B match the CPU oracle.
 """
 import os
+import re
 import socket
 import subprocess
 import sys
@@ -27,15 +29,18 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_slab_launcher_two_gpus_matches_oracle():
+def test_slab_launcher_multi_gpu_matches_oracle():
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
+    # up to four ranks, so that the ring has a rank with both neighbours
+    world = min(torch.cuda.device_count(), 4)
     env = dict(os.environ, GEMM_LAUNCH_LOG="0")
     cmd = ["timeout", "-k", "60", "400", sys.executable, "-m", "torch.distributed.run",
-           "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1",
+           "--nnodes=1", f"--nproc-per-node={world}", "--master-addr", "127.0.0.1",
            "--master-port", str(_free_port()), str(REPO / "tests" / "nccl_slab_worker.py")]
     proc = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=500)
-    lines = [ln for ln in proc.stdout.splitlines() if ln.startswith("RESULT ")]
+    lines = re.findall(r"RESULT \d+ .*", proc.stdout)
     assert proc.returncode == 0, proc.stdout[-4000:] + proc.stderr[-4000:]
-    assert sorted(lines) == ["RESULT 0 ok", "RESULT 1 ok"], "\n".join(lines) + proc.stderr[-3000:]
+    assert sorted(lines) == [f"RESULT {r} ok" for r in range(world)], \
+        "\n".join(lines) + proc.stderr[-3000:]
