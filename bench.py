@@ -567,7 +567,7 @@ def verify_rank(sets, b_dev, alpha, rank, world, rows=256, spots=64):
 
 def run_multi(args, gb, cfgs, device, pk, rank, world):
     import torch.distributed as dist
-    from gemm_b200.slab import SlabGemm
+    from gemm_b200.slab import PeerRing, SlabGemm
     cfg = cfgs["sharded32768"]
     slab_m = cfg["m"] // 8  # 4096 rows per rank: the 8-GPU partition of the config
     m_total = slab_m * world
@@ -604,13 +604,15 @@ def run_multi(args, gb, cfgs, device, pk, rank, world):
     bcast_ms = min(bcast_times)
     del warm
     # every rank holds the same B: a position-weighted checksum of its bits
-    bits = b.view(torch.int16)
-    row_w = torch.arange(1, k + 1, device=device, dtype=torch.float64)
-    col_w = torch.arange(1, n + 1, device=device, dtype=torch.float64)
-    csum = [float((bits.sum(dim=1, dtype=torch.int64).double() * row_w).sum().item()),
-            float((bits.sum(dim=0, dtype=torch.int64).double() * col_w).sum().item())]
-    b_same = all(max_over_ranks(x) == max_over_ranks(x, dist.ReduceOp.MIN) for x in csum)
-    del bits, row_w, col_w
+    def b_checksum(t):
+        bits = t.view(torch.int16)
+        row_w = torch.arange(1, k + 1, device=device, dtype=torch.float64)
+        col_w = torch.arange(1, n + 1, device=device, dtype=torch.float64)
+        return [float((bits.sum(dim=1, dtype=torch.int64).double() * row_w).sum().item()),
+                float((bits.sum(dim=0, dtype=torch.int64).double() * col_w).sum().item())]
+
+    b_sum0 = b_checksum(b)
+    b_same = all(max_over_ranks(x) == max_over_ranks(x, dist.ReduceOp.MIN) for x in b_sum0)
     # this rank's A slab (seed = rank) and C slab (zero)
     g = torch.Generator(device=device).manual_seed(1 + rank)
     a = (torch.randn((slab_m, k), generator=g, device=device) / math.sqrt(k)).half()
@@ -696,6 +698,30 @@ def run_multi(args, gb, cfgs, device, pk, rank, world):
     ov_ms = overlapped(a, c_ov, 3)
     same = max_over_ranks(1.0 if torch.equal(c_ov, c_plain) else 0.0, dist.ReduceOp.MIN)
 
+    # the same with B along a ring of copy-engine peer copies (PeerRing): the
+    # GEMM keeps all SMs but one pair while B's chunks land. It rewrites every
+    # non-source replica with B, which the plain steps above already used.
+    ring = PeerRing(b, timeout_s=30.0)
+
+    def ring_overlapped(a_s, c_s, reps):
+        times = []
+        for _ in range(reps):
+            dist.barrier()
+            torch.cuda.synchronize()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+            ring.broadcast_and_run(a_s, c_s, alpha, beta)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            times.append(max_over_ranks(ev0.elapsed_time(ev1)))
+        return min(times)
+
+    c_ring = torch.empty_like(c)
+    ring_overlapped(a, c_ring, 1)  # warm-up (first calls map nothing new, but load the flag kernel)
+    ring_ms = ring_overlapped(a, c_ring, 3)
+    ring_same = max_over_ranks(1.0 if torch.equal(c_ring, c_plain) else 0.0, dist.ReduceOp.MIN)
+    ring_b_same = max_over_ranks(1.0 if b_checksum(b) == b_sum0 else 0.0, dist.ReduceOp.MIN)
+
     # strong scaling: the fixed 32768-row problem on `world` GPUs (this rank's
     # share of the rows, broadcast of B overlapped), against the whole problem
     # on one GPU (rank 0 alone, B already resident: nothing to broadcast)
@@ -704,7 +730,9 @@ def run_multi(args, gb, cfgs, device, pk, rank, world):
     g = torch.Generator(device=device).manual_seed(100 + rank)
     a_fix = (torch.randn((rows_fix, k), generator=g, device=device) / math.sqrt(k)).half()
     c_fix = torch.zeros((rows_fix, n), device=device, dtype=torch.float16)
-    overlapped(a_fix, c_fix, 1)  # warm-up at this size
+    c_fix_nccl = torch.zeros_like(c_fix)
+    overlapped(a_fix, c_fix_nccl, 1)  # warm-up at this size
+    ring_overlapped(a_fix, c_fix, 1)
     a_all = c_all = None
     if rank == 0:
         g = torch.Generator(device=device).manual_seed(7)
@@ -712,14 +740,17 @@ def run_multi(args, gb, cfgs, device, pk, rank, world):
         c_all = torch.zeros((m_fix, n), device=device, dtype=torch.float16)
         gb.gemm(a_all, b, c_all, alpha, beta)
     # the N-GPU time and the one-GPU time in alternating blocks (same clock state)
-    strong, one_gpu = [], []
+    strong, strong_nccl, one_gpu = [], [], []
     for _ in range(2):
-        strong.append(overlapped(a_fix, c_fix, 1))
+        strong.append(ring_overlapped(a_fix, c_fix, 1))
+        strong_nccl.append(overlapped(a_fix, c_fix_nccl, 1))
         dist.barrier()
         t1 = time_block(lambda: gb.gemm(a_all, b, c_all, alpha, beta), 2) if rank == 0 else 0.0
         one_gpu.append(max_over_ranks(t1))
-    strong_ms, t1_ms = min(strong), min(one_gpu)
+    strong_ms, strong_nccl_ms, t1_ms = min(strong), min(strong_nccl), min(one_gpu)
     del a_all, c_all
+    torch.cuda.synchronize()
+    ring.close()
     dist.destroy_process_group(bgroup)
     st = gb.status()
     if st != 0:
@@ -727,14 +758,15 @@ def run_multi(args, gb, cfgs, device, pk, rank, world):
 
     # every rank's results against the CPU oracle (outside every timed region)
     ver = verify_rank([("steps", a, c_plain), ("overlapped_broadcast", a, c_ov),
-                       ("strong_scaling", a_fix, c_fix)], b, alpha, rank, world)
+                       ("ring_overlapped", a, c_ring), ("strong_scaling", a_fix, c_fix),
+                       ("strong_scaling_nccl", a_fix, c_fix_nccl)], b, alpha, rank, world)
     ver_all = {}
     for name, v in ver.items():
         ver_all[name] = {"pass": bool(max_over_ranks(1.0 if v["pass"] else 0.0, dist.ReduceOp.MIN)),
                          "max_scaled": max_over_ranks(v["max_scaled"]),
                          "rel_frob": max_over_ranks(v["rel_frob"]),
                          "fp64_spot_max_scaled": max_over_ranks(v["fp64_spot_max_scaled"])}
-    verified = all(v["pass"] for v in ver_all.values()) and b_same
+    verified = all(v["pass"] for v in ver_all.values()) and b_same and bool(ring_b_same)
     per_gpu = value / world
     alone_tflops = 2.0 * slab_m * n * k / alone_ms / 1e9
     conc_per_gpu = 2.0 * slab_m * n * k / conc_ms / 1e9
@@ -770,7 +802,16 @@ def run_multi(args, gb, cfgs, device, pk, rank, world):
                           "ms_max_over_ranks": round(ov_ms, 3),
                           "sequential_ms": round(bcast_ms + ms_v, 3),
                           "chunks": args.bcast_chunks, "reserve_sms": args.bcast_reserve_sms,
-                          "c_identical_to_plain_path": bool(same)}},
+                          "c_identical_to_plain_path": bool(same)},
+                      "ring_overlapped_with_gemm": {
+                          "ms_max_over_ranks": round(ring_ms, 3),
+                          "gemm_alone_ms": round(ms_v, 3),
+                          "vs_gemm_alone": round(ring_ms / ms_v, 4),
+                          "chunks": len(ring.bounds), "blocks": len(ring.block_layout(slab_m)[1]),
+                          "c_identical_to_plain_path": bool(ring_same),
+                          "b_identical_after": bool(ring_b_same),
+                          "method": "PeerRing: B's column chunks along a ring of copy-engine "
+                                    "peer copies, each GEMM block as its chunks land"}},
         "scaling_detail": {
             "slab_alone_ms": round(alone_ms, 4), "slab_alone_tflops": round(alone_tflops, 2),
             "slab_all_ranks_ms": round(conc_ms, 4), "per_gpu_tflops": round(conc_per_gpu, 2),
@@ -782,9 +823,12 @@ def run_multi(args, gb, cfgs, device, pk, rank, world):
             "strong": {"problem": f"{m_fix}x{n}x{k}", "one_gpu_ms": round(t1_ms, 3),
                        "n_gpu_ms_with_broadcast": round(strong_ms, 3),
                        "efficiency": round(t1_ms / (world * strong_ms), 4),
+                       "n_gpu_ms_nccl_broadcast": round(strong_nccl_ms, 3),
+                       "efficiency_nccl_broadcast": round(t1_ms / (world * strong_nccl_ms), 4),
                        "method": "one GPU: the whole problem on rank 0 (B resident); N GPUs: "
-                                 "32768/N rows per rank with B's broadcast overlapped "
-                                 "(broadcast_and_run); best of 2 alternating blocks each"}},
+                                 "32768/N rows per rank with B's replication overlapped "
+                                 "(PeerRing; NCCL broadcast_and_run beside it); best of 2 "
+                                 "alternating blocks each"}},
         "clocks": clk.summary(),
     }
 
