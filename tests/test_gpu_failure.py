@@ -4,7 +4,8 @@ Every spin-wait in the library's kernels is bounded. The self-test kernel
 waits on an mbarrier that nothing completes; with a 1 ms bound it must record
 code 5 in the device error word and return (status 1005), leaving the context
 usable for the next GEMM. The real tile kernels are run with their operand
-feed switched off, so that their own waits run out the same way. No trap,
+feed switched off, so that their own waits run out the same way, and the
+multi-GPU ring's flag kernel waits on a flag word nothing sets. No trap,
 assert, bad address or endless loop is used.
 """
 import pytest
@@ -58,3 +59,33 @@ def test_tile_kernel_bounded_waits_unwind(lib, cuda, path, tile_n, shape):
     assert bool((gc.tensor == 7.0).all()) and gc.canaries_ok(), "C written by a stalled kernel"
     c, a, b, c0 = run(lib, cuda, m, n, k, 0.75, 0.5, path=path, tile_n=tile_n)
     assert verify(c, a, b, c0, 0.75, 0.5).passed
+
+
+def test_peer_flag_wait_bounded(lib, cuda):
+    """The copy-engine ring's flag kernel (gemm_peer_flags) on one GPU with a
+    flag word that nothing sets: the bounded wait must record code 6 (status
+    1006) and return; a second wait issued before the status is read must skip
+    its wait (so a failed ring drains fast) instead of sitting out its own 5 s
+    bound; after the read, a signal followed by a satisfied wait reports
+    nothing. Only this process's own flag words are touched."""
+    import time
+    import torch
+
+    flags = torch.zeros(2, dtype=torch.int32, device=cuda)
+    stream = torch.cuda.current_stream().cuda_stream
+    p0, p1 = flags.data_ptr(), flags.data_ptr() + 4
+    assert lib.gemm_launcher_status() == 0
+    t0 = time.monotonic()
+    assert lib.gemm_peer_flags(None, 0, None, 0, p0, 1, None, 0, 1000, stream) == 0
+    assert lib.gemm_peer_flags(None, 0, None, 0, p0, 1, None, 0, 5_000_000, stream) == 0
+    torch.cuda.synchronize()
+    assert time.monotonic() - t0 < 2.5
+    assert lib.gemm_launcher_status() == 1006
+    assert lib.gemm_launcher_status() == 0
+    # signal word 1 to 7, then wait for word 1 >= 7 and word 0 >= 0: satisfied
+    assert lib.gemm_peer_flags(p1, 7, None, 0, p1, 7, p0, 0, 1_000_000, stream) == 0
+    torch.cuda.synchronize()
+    assert lib.gemm_launcher_status() == 0
+    assert flags.tolist() == [0, 7]
+    c, a, b, c0 = run(lib, cuda, 256, 512, 192, 1.0, 0.5, fn="launcher")
+    assert verify(c, a, b, c0, 1.0, 0.5).passed
