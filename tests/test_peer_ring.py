@@ -124,7 +124,7 @@ def simulate(world, n_chunks, cpb, calls, seed, program=ring_program):
     return True
 
 
-@pytest.mark.parametrize("world", [1, 2, 3, 5])
+@pytest.mark.parametrize("world", [1, 2, 3, 5, 8])
 @pytest.mark.parametrize("n_chunks,cpb", [(1, 1), (3, 1), (7, 2), (8, 4), (5, 8)])
 def test_ring_protocol_random_interleavings(world, n_chunks, cpb):
     for seed in range(40):
@@ -198,3 +198,15 @@ def test_simulator_catches_planted_bugs(bug):
         except RingViolation:
             caught += 1
     assert caught > 0
+
+
+def test_peer_ring_rejects_host_and_strided_replicas():
+    """The replica must be a contiguous FP16 CUDA tensor; checked before any
+    collective, so a bad argument fails on the calling rank alone."""
+    import torch
+    from gemm_b200.slab import PeerRing
+
+    with pytest.raises(ValueError):
+        PeerRing(torch.zeros((16, 32), dtype=torch.float16))          # host memory
+    with pytest.raises(ValueError):
+        PeerRing(torch.zeros((16, 32), dtype=torch.float32))
